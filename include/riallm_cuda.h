@@ -1,0 +1,197 @@
+/*
+ * riallm_cuda.h -- C ABI of libriallm_cuda.so, the B200 (sm_100a) engine for
+ * riallm's mixture-of-experts block forward with block-quantized weights.
+ *
+ * Plain pointers and sizes only: no C++ or torch types cross this boundary.
+ * Every function returns riallm_status (0 = ok) unless it returns a size.
+ * Device pointers are caller-owned unless a function says it allocates; the
+ * library never frees caller memory. All work is asynchronous on the given
+ * CUDA stream (a cudaStream_t passed as void*, NULL = legacy default stream).
+ * One context per device per host thread.
+ *
+ * The reference (riallm, Rust) has no FFI of its own: each entry point below
+ * names the reference function it stands in for (file:line inside the
+ * riallm crate). A Rust `riallm-cuda` crate binds these with `extern "C"`.
+ */
+#ifndef RIALLM_CUDA_H
+#define RIALLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RIALLM_CUDA_ABI_VERSION 1
+
+/* Status codes. 1-4 map onto RiallmError variants (src/error.rs:8-47). */
+typedef enum riallm_status {
+  RIALLM_OK = 0,
+  RIALLM_ERR_MEMORY = 1,        /* RiallmError::Memory */
+  RIALLM_ERR_QUANTIZATION = 2,  /* RiallmError::Quantization */
+  RIALLM_ERR_CONFIG = 3,        /* RiallmError::Config */
+  RIALLM_ERR_MODEL_LOADING = 4, /* RiallmError::ModelLoading ("Tensor not found") */
+  RIALLM_ERR_CUDA = 5,          /* device/runtime failure (RiallmError::Candle's role) */
+  RIALLM_ERR_TIMEOUT = 6,       /* a bounded device-side wait expired */
+  RIALLM_ERR_INVALID = 7        /* NULL or malformed argument */
+} riallm_status;
+
+/* CompressionType, src/config.rs:323-332. */
+typedef enum riallm_compression {
+  RIALLM_COMPRESSION_NONE = 0,     /* data is float32[numel] */
+  RIALLM_COMPRESSION_FOUR_BIT = 1, /* NF4, 64-element blocks, 2 codes per byte */
+  RIALLM_COMPRESSION_EIGHT_BIT = 2 /* 8-bit affine, 128-element blocks */
+} riallm_compression;
+
+typedef enum riallm_dtype {
+  RIALLM_DTYPE_F32 = 0,
+  RIALLM_DTYPE_BF16 = 1
+} riallm_dtype;
+
+/* Dequantization semantics.
+ * REFERENCE: exactly src/quantization.rs:45-95 ((code - zero) * scale; an
+ *   NF4 element at position 63 of its block uses the next block's scale and
+ *   zero, and the tensor's last element falls back to scale 1, zero 0).
+ * CODEBOOK: NF4 table[code] * scale (the intended NF4 decode); for 8-bit,
+ *   code * scale + zero (the inverse of the quantizer). */
+typedef enum riallm_dequant_mode {
+  RIALLM_DEQUANT_REFERENCE = 0,
+  RIALLM_DEQUANT_CODEBOOK = 1
+} riallm_dequant_mode;
+
+/* QuantizedTensor, src/quantization.rs:12-30, as device pointers. The
+ * tensor's elements run over the flattened shape. */
+typedef struct riallm_qtensor {
+  int32_t qtype;             /* riallm_compression */
+  int32_t block_size;        /* 64 (FOUR_BIT) or 128 (EIGHT_BIT) */
+  const void* data;          /* packed codes, or float32 when qtype == NONE */
+  const float* scales;       /* scales.len() == n_scales */
+  const float* zero_points;  /* zero_points.len() == n_zero_points */
+  uint64_t numel;            /* shape.iter().product() */
+  uint64_t n_scales;
+  uint64_t n_zero_points;
+} riallm_qtensor;
+
+/* One layer's MoE tensors (names as src/model.rs:762,791-792,825-831). */
+typedef struct riallm_moe_weights {
+  riallm_qtensor gate;               /* mlp.gate.weight            [E, H]     */
+  riallm_qtensor gate_up_proj;       /* mlp.experts.gate_up_proj   [E, 2I, H] */
+  riallm_qtensor down_proj;          /* mlp.experts.down_proj      [E, H, I]  */
+  /* Optional Qwen3.5 shared expert; leave data == NULL when absent. */
+  riallm_qtensor shared_gate_proj;   /* [Is, H] */
+  riallm_qtensor shared_up_proj;     /* [Is, H] */
+  riallm_qtensor shared_down_proj;   /* [H, Is] */
+  riallm_qtensor shared_expert_gate; /* [1, H]  */
+  int32_t shared_intermediate;       /* Is */
+} riallm_moe_weights;
+
+typedef struct riallm_ctx riallm_ctx;
+
+/* ----------------------------------------------------------- context */
+
+int32_t riallm_cuda_abi_version(void);
+
+/* Creates a context on CUDA device `device` (DeviceSpec::Cuda(id),
+ * src/config.rs:350-372; src/model.rs:100-104 picks the device). */
+int32_t riallm_cuda_ctx_create(int32_t device, riallm_ctx** out);
+int32_t riallm_cuda_ctx_destroy(riallm_ctx* ctx);
+
+/* Message of the last failure on this context ("" when none). */
+const char* riallm_cuda_last_error(const riallm_ctx* ctx);
+
+/* ------------------------------------------------------------ memory
+ * src/memory.rs:60-78 (get_memory_stats), :113-125 (move_tensors_to_device),
+ * :183-198 (synchronize_device). */
+
+int32_t riallm_cuda_alloc(riallm_ctx* ctx, uint64_t bytes, void** dptr);
+int32_t riallm_cuda_free(riallm_ctx* ctx, void* dptr);
+int32_t riallm_cuda_host_alloc_pinned(riallm_ctx* ctx, uint64_t bytes, void** hptr);
+int32_t riallm_cuda_host_free_pinned(riallm_ctx* ctx, void* hptr);
+int32_t riallm_cuda_memcpy_h2d_async(riallm_ctx* ctx, void* dst, const void* src,
+                                     uint64_t bytes, void* stream);
+int32_t riallm_cuda_memcpy_d2h_async(riallm_ctx* ctx, void* dst, const void* src,
+                                     uint64_t bytes, void* stream);
+int32_t riallm_cuda_stream_synchronize(riallm_ctx* ctx, void* stream);
+int32_t riallm_cuda_memory_stats(riallm_ctx* ctx, uint64_t* free_bytes,
+                                 uint64_t* total_bytes);
+
+/* ------------------------------------------------------ quantization */
+
+/* Number of scale/zero blocks and packed data bytes for numel elements. */
+uint64_t riallm_quant_num_blocks(int32_t qtype, uint64_t numel);
+uint64_t riallm_quant_data_bytes(int32_t qtype, uint64_t numel);
+
+/* quantize_tensor (src/quantization.rs:99-107 -> :111-176 NF4,
+ * :199-245 8-bit), bit-identical to the reference's host loops.
+ * src: float32[numel] on the device; outputs sized by the helpers above. */
+int32_t riallm_cuda_quantize(riallm_ctx* ctx, int32_t qtype, const float* src,
+                             uint64_t numel, uint8_t* data, float* scales,
+                             float* zero_points, void* stream);
+
+/* QuantizedTensor::dequantize (src/quantization.rs:34-95). dst holds numel
+ * values of dst_dtype (bf16 values are the float32 results rounded to
+ * nearest even). NF4 requires data length ceil(numel/2). */
+int32_t riallm_cuda_dequantize(riallm_ctx* ctx, const riallm_qtensor* t,
+                               int32_t mode, void* dst, int32_t dst_dtype,
+                               void* stream);
+
+/* --------------------------------------------------------- MoE block */
+
+#define RIALLM_MOE_ADD_TO_OUT 1u /* out += block(x) instead of out = block(x) */
+
+/* apply_qwen3_5_moe (src/model.rs:751-818, shared expert :820-834):
+ * router matmul -> softmax -> stable top-k -> renormalise -> per-expert
+ * SwiGLU (gate = rows [0,I) of gate_up_proj[e], up = rows [I,2I)) -> down
+ * projection -> routing-weight scale -> sum in expert-ascending order
+ * (+ shared expert). x and out are [T,H] in act_dtype. Expert tensors must be
+ * FOUR_BIT or EIGHT_BIT; gate/shared tensors may be any compression.
+ * Shape limits: H % 256 == 0, I % 256 == 0, E <= 256, k <= 16, k <= E.
+ * Scratch comes from the context's device arena, which grows with
+ * cudaMalloc on demand (see riallm_cuda_moe_reserve). */
+int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w,
+                                const void* x, void* out, int32_t T, int32_t H,
+                                int32_t I, int32_t E, int32_t k,
+                                int32_t act_dtype, uint32_t flags, void* stream);
+
+/* Grows the context's scratch arena for blocks up to these sizes now, so
+ * that later riallm_cuda_moe_forward calls allocate nothing. */
+int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I,
+                                int32_t E, int32_t k, int32_t act_dtype);
+
+/* Router and bucketing only (src/model.rs:762-789), for bit-exact checks.
+ * topk_idx/topk_w [T,k]; counts [E]; offsets [E+1]; perm_pair [T*k]
+ * (pair ids t*k+j grouped by expert ascending, token-ascending within an
+ * expert). Any output except topk_idx may be NULL. */
+int32_t riallm_cuda_moe_route(riallm_ctx* ctx, const riallm_qtensor* gate,
+                              const void* x, int32_t T, int32_t H, int32_t E,
+                              int32_t k, int32_t act_dtype, int32_t* topk_idx,
+                              float* topk_w, int32_t* counts, int32_t* offsets,
+                              int32_t* perm_pair, void* stream);
+
+/* ---------------------------------------------------------- profiling
+ * The reference's Profiler (src/profiler.rs:75-96) times each layer on the
+ * host wall clock. Here, when enabled, riallm_cuda_moe_forward records a
+ * CUDA event pair around each phase on the call's stream; reading
+ * synchronizes, returns the accumulated device milliseconds per phase since
+ * the last read, and resets them. The launch counter counts every kernel
+ * this context has launched (never reset). */
+typedef enum riallm_phase {
+  RIALLM_PHASE_ROUTE = 0,    /* router weight decode + router + permutation */
+  RIALLM_PHASE_GATHER = 1,   /* token rows into expert order */
+  RIALLM_PHASE_GATE_UP = 2,  /* expert gate/up GEMM + SwiGLU */
+  RIALLM_PHASE_DOWN = 3,     /* expert down GEMM */
+  RIALLM_PHASE_SHARED = 4,   /* shared expert */
+  RIALLM_PHASE_COMBINE = 5,  /* weighted combine */
+  RIALLM_NUM_PHASES = 6
+} riallm_phase;
+
+int32_t riallm_cuda_profile_enable(riallm_ctx* ctx, int32_t enable);
+int32_t riallm_cuda_profile_read(riallm_ctx* ctx, float* ms_per_phase,
+                                 uint64_t* calls);
+uint64_t riallm_cuda_launch_count(const riallm_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RIALLM_CUDA_H */

@@ -1,0 +1,630 @@
+// api.cu -- the extern "C" entry points of libriallm_cuda (include/riallm_cuda.h).
+//
+// Orchestrates one MoE block call (src/model.rs:751-818) as a fixed sequence
+// of launches on the caller's stream, with no host synchronisation:
+//   dequant router weights -> router/top-k -> counting-sort permutation ->
+//   gather tokens -> expert GEMMs (tcgen05 for bf16 activations, CUDA cores
+//   for float32) -> [shared expert] -> weighted combine.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "internal.h"
+
+using rl::MoeLayout;
+
+namespace {
+
+int set_err(riallm_ctx* ctx, int code, const std::string& msg) {
+  if (ctx) ctx->last_error = msg;
+  return code;
+}
+
+int cuda_err(riallm_ctx* ctx, cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return RIALLM_OK;
+  std::string m = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  if (e == cudaErrorMemoryAllocation) return set_err(ctx, RIALLM_ERR_MEMORY, m);
+  return set_err(ctx, RIALLM_ERR_CUDA, m);
+}
+
+#define RL_CUDA(ctx, call, what)                 \
+  do {                                           \
+    cudaError_t _e = (call);                     \
+    if (_e != cudaSuccess) return cuda_err(ctx, _e, what); \
+  } while (0)
+
+inline uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Checks a QuantizedTensor descriptor against its expected element count.
+int check_qtensor(riallm_ctx* ctx, const riallm_qtensor& t, uint64_t numel, const char* name,
+                  bool need_quantized) {
+  if (t.data == nullptr) return set_err(ctx, RIALLM_ERR_MODEL_LOADING, std::string("Tensor not found: ") + name);
+  if (t.numel != numel)
+    return set_err(ctx, RIALLM_ERR_CONFIG, std::string(name) + ": numel " + std::to_string(t.numel) +
+                                               " != expected " + std::to_string(numel));
+  if (t.qtype == RIALLM_COMPRESSION_NONE) {
+    if (need_quantized)
+      return set_err(ctx, RIALLM_ERR_QUANTIZATION, std::string(name) + ": expert weights must be FourBit or EightBit");
+    return RIALLM_OK;
+  }
+  if (t.qtype != RIALLM_COMPRESSION_FOUR_BIT && t.qtype != RIALLM_COMPRESSION_EIGHT_BIT)
+    return set_err(ctx, RIALLM_ERR_QUANTIZATION, std::string(name) + ": unknown qtype");
+  const int want_bs = t.qtype == RIALLM_COMPRESSION_FOUR_BIT ? 64 : 128;
+  if (t.block_size != want_bs)
+    return set_err(ctx, RIALLM_ERR_QUANTIZATION,
+                   std::string(name) + ": block_size " + std::to_string(t.block_size) + " unsupported");
+  if (t.scales == nullptr || t.zero_points == nullptr)
+    return set_err(ctx, RIALLM_ERR_QUANTIZATION, std::string(name) + ": missing scales/zero_points");
+  if (!aligned16(t.data) || !aligned16(t.scales) || !aligned16(t.zero_points))
+    return set_err(ctx, RIALLM_ERR_INVALID, std::string(name) + ": device buffers must be 16-byte aligned");
+  return RIALLM_OK;
+}
+
+int ensure_arena(riallm_ctx* ctx, uint64_t bytes) {
+  if (ctx->arena_bytes >= bytes) return RIALLM_OK;
+  if (ctx->arena) {
+    RL_CUDA(ctx, cudaFree(ctx->arena), "cudaFree(arena)");
+    ctx->arena = nullptr;
+    ctx->arena_bytes = 0;
+  }
+  const uint64_t sz = align_up(bytes, 2u << 20);
+  RL_CUDA(ctx, cudaMalloc(&ctx->arena, sz), "cudaMalloc(arena)");
+  ctx->arena_bytes = sz;
+  return RIALLM_OK;
+}
+
+int set_device(riallm_ctx* ctx) {
+  RL_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  return RIALLM_OK;
+}
+
+// Phase profiling: an event pair per phase per call when enabled.
+cudaEvent_t take_event(riallm_ctx* ctx) {
+  if (!ctx->event_pool.empty()) {
+    cudaEvent_t e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+struct PhaseScope {
+  riallm_ctx* ctx;
+  cudaStream_t st;
+  int phase;
+  cudaEvent_t start = nullptr;
+  PhaseScope(riallm_ctx* c, cudaStream_t s, int p) : ctx(c), st(s), phase(p) {
+    if (ctx->profiling && (start = take_event(ctx))) cudaEventRecord(start, st);
+  }
+  ~PhaseScope() {
+    if (!start) return;
+    cudaEvent_t stop = take_event(ctx);
+    if (!stop) {
+      ctx->event_pool.push_back(start);
+      return;
+    }
+    cudaEventRecord(stop, st);
+    ctx->pending.push_back({phase, start, stop});
+  }
+};
+
+}  // namespace
+
+namespace rl {
+
+MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int shared_I) {
+  MoeLayout L{};
+  const uint64_t P = (uint64_t)T * k;
+  const uint64_t a = 1024;
+  const uint64_t esz = act_dtype == RIALLM_DTYPE_BF16 ? 2 : 4;
+  uint64_t o = 0;
+  auto take = [&](uint64_t bytes) {
+    uint64_t r = o;
+    o = align_up(o + bytes, a);
+    return r;
+  };
+  L.wg = take((uint64_t)E * H * 4);
+  L.topk_idx = take(P * 4);
+  L.topk_w = take(P * 4);
+  L.counts = take((uint64_t)E * 4);
+  L.offsets = take((uint64_t)(E + 1) * 4);
+  L.perm_pair = take(P * 4);
+  L.inv_pos = take(P * 4);
+  L.x_perm = take(P * H * esz);
+  L.h_perm = take(P * I * esz);
+  L.y_perm = take(P * H * 4);
+  L.proj = act_dtype == RIALLM_DTYPE_BF16 ? take(0) : take(P * 2 * (uint64_t)I * 4);
+  if (shared_I > 0) {
+    L.sh_g = take((uint64_t)T * shared_I * 4);
+    L.sh_u = take((uint64_t)T * shared_I * 4);
+    L.sh_h = take((uint64_t)T * shared_I * esz);
+    L.sh_y = take((uint64_t)T * H * 4);
+    L.sh_gate = take((uint64_t)T * 4);
+  }
+  L.total = o + a;
+  return L;
+}
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                              CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                              CUtensorMapFloatOOBfill);
+
+CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                              uint64_t dim0, uint64_t dim1, uint64_t row_stride_bytes,
+                              uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle) {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  if (!fn) return CUDA_ERROR_NOT_FOUND;
+  const cuuint64_t dims[2] = {dim0, dim1};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box0, box1};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+}  // namespace rl
+
+extern "C" {
+
+int32_t riallm_cuda_abi_version(void) { return RIALLM_CUDA_ABI_VERSION; }
+
+int32_t riallm_cuda_ctx_create(int32_t device, riallm_ctx** out) {
+  if (!out) return RIALLM_ERR_INVALID;
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || device < 0 || device >= n) return RIALLM_ERR_CONFIG;
+  riallm_ctx* ctx = new riallm_ctx();
+  ctx->device = device;
+  if (cudaSetDevice(device) != cudaSuccess) {
+    delete ctx;
+    return RIALLM_ERR_CUDA;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) {
+    delete ctx;
+    return RIALLM_ERR_CUDA;
+  }
+  if (prop.major != 10) {
+    delete ctx;
+    return RIALLM_ERR_CONFIG;  // sm_100a only
+  }
+  ctx->num_sms = prop.multiProcessorCount;
+  if (cudaMalloc(&ctx->d_status, sizeof(int)) != cudaSuccess ||
+      cudaMemset(ctx->d_status, 0, sizeof(int)) != cudaSuccess) {
+    delete ctx;
+    return RIALLM_ERR_MEMORY;
+  }
+  *out = ctx;
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_ctx_destroy(riallm_ctx* ctx) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  if (ctx->arena) cudaFree(ctx->arena);
+  if (ctx->d_status) cudaFree(ctx->d_status);
+  for (auto& pe : ctx->pending) {
+    cudaEventDestroy(pe.start);
+    cudaEventDestroy(pe.stop);
+  }
+  for (cudaEvent_t e : ctx->event_pool) cudaEventDestroy(e);
+  delete ctx;
+  return RIALLM_OK;
+}
+
+const char* riallm_cuda_last_error(const riallm_ctx* ctx) {
+  return ctx ? ctx->last_error.c_str() : "null context";
+}
+
+int32_t riallm_cuda_alloc(riallm_ctx* ctx, uint64_t bytes, void** dptr) {
+  if (!ctx || !dptr) return RIALLM_ERR_INVALID;
+  if (int s = set_device(ctx)) return s;
+  RL_CUDA(ctx, cudaMalloc(dptr, bytes), "cudaMalloc");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_free(riallm_ctx* ctx, void* dptr) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaFree(dptr), "cudaFree");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_host_alloc_pinned(riallm_ctx* ctx, uint64_t bytes, void** hptr) {
+  if (!ctx || !hptr) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaHostAlloc(hptr, bytes, cudaHostAllocDefault), "cudaHostAlloc");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_host_free_pinned(riallm_ctx* ctx, void* hptr) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaFreeHost(hptr), "cudaFreeHost");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_memcpy_h2d_async(riallm_ctx* ctx, void* dst, const void* src, uint64_t bytes,
+                                     void* stream) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream),
+          "cudaMemcpyAsync(H2D)");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_memcpy_d2h_async(riallm_ctx* ctx, void* dst, const void* src, uint64_t bytes,
+                                     void* stream) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream),
+          "cudaMemcpyAsync(D2H)");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_stream_synchronize(riallm_ctx* ctx, void* stream) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaStreamSynchronize((cudaStream_t)stream), "cudaStreamSynchronize");
+  int st = 0;
+  RL_CUDA(ctx, cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost), "status read");
+  if (st != 0) {
+    cudaMemset(ctx->d_status, 0, sizeof(int));
+    return set_err(ctx, st, "a bounded device-side wait expired (kernel aborted)");
+  }
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_memory_stats(riallm_ctx* ctx, uint64_t* free_bytes, uint64_t* total_bytes) {
+  if (!ctx || !free_bytes || !total_bytes) return RIALLM_ERR_INVALID;
+  if (int s = set_device(ctx)) return s;
+  size_t f = 0, t = 0;
+  RL_CUDA(ctx, cudaMemGetInfo(&f, &t), "cudaMemGetInfo");
+  *free_bytes = f;
+  *total_bytes = t;
+  return RIALLM_OK;
+}
+
+uint64_t riallm_quant_num_blocks(int32_t qtype, uint64_t numel) {
+  if (qtype == RIALLM_COMPRESSION_FOUR_BIT) return (numel + 63) / 64;
+  if (qtype == RIALLM_COMPRESSION_EIGHT_BIT) return (numel + 127) / 128;
+  return 0;
+}
+
+uint64_t riallm_quant_data_bytes(int32_t qtype, uint64_t numel) {
+  if (qtype == RIALLM_COMPRESSION_FOUR_BIT) return (numel + 1) / 2;
+  if (qtype == RIALLM_COMPRESSION_EIGHT_BIT) return numel;
+  return numel * 4;
+}
+
+int32_t riallm_cuda_quantize(riallm_ctx* ctx, int32_t qtype, const float* src, uint64_t numel,
+                             uint8_t* data, float* scales, float* zero_points, void* stream) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  if (qtype != RIALLM_COMPRESSION_FOUR_BIT && qtype != RIALLM_COMPRESSION_EIGHT_BIT)
+    return set_err(ctx, RIALLM_ERR_QUANTIZATION, "No compression specified");
+  if (!src || !data || !scales || !zero_points) return set_err(ctx, RIALLM_ERR_INVALID, "null buffer");
+  if (numel == 0) return RIALLM_OK;
+  if (int s = set_device(ctx)) return s;
+  RL_CUDA(ctx, rl::launch_quantize(qtype, src, numel, data, scales, zero_points, ctx->num_sms,
+                                   (cudaStream_t)stream),
+          "quantize launch");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_dequantize(riallm_ctx* ctx, const riallm_qtensor* t, int32_t mode, void* dst,
+                               int32_t dst_dtype, void* stream) {
+  if (!ctx || !t || !dst) return RIALLM_ERR_INVALID;
+  if (t->qtype != RIALLM_COMPRESSION_NONE && t->qtype != RIALLM_COMPRESSION_FOUR_BIT &&
+      t->qtype != RIALLM_COMPRESSION_EIGHT_BIT)
+    return set_err(ctx, RIALLM_ERR_QUANTIZATION, "unknown qtype");
+  if (t->qtype == RIALLM_COMPRESSION_NONE && mode == RIALLM_DEQUANT_REFERENCE)
+    return set_err(ctx, RIALLM_ERR_QUANTIZATION, "Tensor is not quantized");
+  if (t->qtype != RIALLM_COMPRESSION_NONE && (t->block_size <= 0 || (t->qtype == RIALLM_COMPRESSION_FOUR_BIT && (t->block_size & 1))))
+    return set_err(ctx, RIALLM_ERR_QUANTIZATION, "block_size must be positive (and even for NF4)");
+  if (t->numel == 0) return RIALLM_OK;
+  if (int s = set_device(ctx)) return s;
+  RL_CUDA(ctx, rl::launch_dequant(*t, mode, dst, dst_dtype, ctx->num_sms, (cudaStream_t)stream),
+          "dequantize launch");
+  return RIALLM_OK;
+}
+
+static int check_shapes(riallm_ctx* ctx, int T, int H, int I, int E, int k) {
+  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "non-positive MoE dimension");
+  if (E > 256 || k > 16 || k > E)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "need E <= 256, k <= 16, k <= E");
+  if (H % 256 != 0 || I % 256 != 0)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "need hidden % 256 == 0 and intermediate % 256 == 0");
+  if ((int64_t)T * k > (1ll << 24)) return set_err(ctx, RIALLM_ERR_CONFIG, "too many tokens");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I, int32_t E,
+                                int32_t k, int32_t act_dtype) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  if (int s = check_shapes(ctx, T, H, I, E, k)) return s;
+  if (int s = set_device(ctx)) return s;
+  MoeLayout L = rl::moe_layout(T, H, I, E, k, act_dtype, 0);
+  return ensure_arena(ctx, L.total);
+}
+
+static int route_into(riallm_ctx* ctx, const riallm_qtensor& gate, const void* x, int T, int H, int E,
+                      int k, bool bf16, char* base, const MoeLayout& L, cudaStream_t st) {
+  const int P = T * k;
+  float* wg = (float*)(base + L.wg);
+  RL_CUDA(ctx, rl::launch_dequant(gate, RIALLM_DEQUANT_REFERENCE, wg, RIALLM_DTYPE_F32, ctx->num_sms, st),
+          "router weight dequant");
+  RL_CUDA(ctx, rl::launch_router(x, bf16, wg, T, H, E, k, (int*)(base + L.topk_idx),
+                                 (float*)(base + L.topk_w), st),
+          "router");
+  RL_CUDA(ctx, rl::launch_permute((int*)(base + L.topk_idx), P, E, (int*)(base + L.counts),
+                                  (int*)(base + L.offsets), (int*)(base + L.perm_pair),
+                                  (int*)(base + L.inv_pos), st),
+          "permute");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_moe_route(riallm_ctx* ctx, const riallm_qtensor* gate, const void* x, int32_t T,
+                              int32_t H, int32_t E, int32_t k, int32_t act_dtype, int32_t* topk_idx,
+                              float* topk_w, int32_t* counts, int32_t* offsets, int32_t* perm_pair,
+                              void* stream) {
+  if (!ctx || !gate) return RIALLM_ERR_INVALID;
+  if ((!x || !topk_idx) && T != 0) return set_err(ctx, RIALLM_ERR_INVALID, "null x/topk_idx");
+  if (T < 0 || H <= 0 || E <= 0 || k <= 0 || E > 256 || k > 16 || k > E || H % 8 != 0)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "router shape out of range");
+  if (int s = check_qtensor(ctx, *gate, (uint64_t)E * H, "mlp.gate.weight", false)) return s;
+  if (T == 0) return RIALLM_OK;
+  if (!aligned16(x)) return set_err(ctx, RIALLM_ERR_INVALID, "x must be 16-byte aligned");
+  if (int s = set_device(ctx)) return s;
+  const bool bf16 = act_dtype == RIALLM_DTYPE_BF16;
+  MoeLayout L = rl::moe_layout(T, H, 256, E, k, act_dtype, 0);
+  if (int s = ensure_arena(ctx, L.total)) return s;
+  char* base = (char*)ctx->arena;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (int s = route_into(ctx, *gate, x, T, H, E, k, bf16, base, L, st)) return s;
+  const uint64_t P = (uint64_t)T * k;
+  RL_CUDA(ctx, cudaMemcpyAsync(topk_idx, base + L.topk_idx, P * 4, cudaMemcpyDeviceToDevice, st), "copy idx");
+  if (topk_w)
+    RL_CUDA(ctx, cudaMemcpyAsync(topk_w, base + L.topk_w, P * 4, cudaMemcpyDeviceToDevice, st), "copy w");
+  if (counts)
+    RL_CUDA(ctx, cudaMemcpyAsync(counts, base + L.counts, (uint64_t)E * 4, cudaMemcpyDeviceToDevice, st),
+            "copy counts");
+  if (offsets)
+    RL_CUDA(ctx, cudaMemcpyAsync(offsets, base + L.offsets, (uint64_t)(E + 1) * 4, cudaMemcpyDeviceToDevice, st),
+            "copy offsets");
+  if (perm_pair)
+    RL_CUDA(ctx, cudaMemcpyAsync(perm_pair, base + L.perm_pair, P * 4, cudaMemcpyDeviceToDevice, st),
+            "copy perm");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x, void* out,
+                                int32_t T, int32_t H, int32_t I, int32_t E, int32_t k, int32_t act_dtype,
+                                uint32_t flags, void* stream) {
+  if (!ctx || !w) return RIALLM_ERR_INVALID;
+  if ((!x || !out) && T != 0) return set_err(ctx, RIALLM_ERR_INVALID, "null x/out");
+  if (act_dtype != RIALLM_DTYPE_BF16 && act_dtype != RIALLM_DTYPE_F32)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "act_dtype must be F32 or BF16");
+  if (int s = check_shapes(ctx, T, H, I, E, k)) return s;
+  if (int s = check_qtensor(ctx, w->gate, (uint64_t)E * H, "mlp.gate.weight", false)) return s;
+  if (int s = check_qtensor(ctx, w->gate_up_proj, (uint64_t)E * 2 * I * H, "mlp.experts.gate_up_proj", true)) return s;
+  if (int s = check_qtensor(ctx, w->down_proj, (uint64_t)E * H * I, "mlp.experts.down_proj", true)) return s;
+  const bool shared = w->shared_gate_proj.data != nullptr;
+  const int Is = shared ? w->shared_intermediate : 0;
+  if (shared) {
+    if (Is <= 0) return set_err(ctx, RIALLM_ERR_CONFIG, "shared_intermediate must be positive");
+    if (int s = check_qtensor(ctx, w->shared_gate_proj, (uint64_t)Is * H, "mlp.shared_expert.gate_proj.weight", false)) return s;
+    if (int s = check_qtensor(ctx, w->shared_up_proj, (uint64_t)Is * H, "mlp.shared_expert.up_proj.weight", false)) return s;
+    if (int s = check_qtensor(ctx, w->shared_down_proj, (uint64_t)H * Is, "mlp.shared_expert.down_proj.weight", false)) return s;
+    if (int s = check_qtensor(ctx, w->shared_expert_gate, (uint64_t)H, "mlp.shared_expert_gate.weight", false)) return s;
+  }
+  if (T == 0) return RIALLM_OK;
+  if (!aligned16(x) || !aligned16(out)) return set_err(ctx, RIALLM_ERR_INVALID, "x/out must be 16-byte aligned");
+  if (int s = set_device(ctx)) return s;
+
+  const bool bf16 = act_dtype == RIALLM_DTYPE_BF16;
+  const int P = T * k;
+  MoeLayout L = rl::moe_layout(T, H, I, E, k, act_dtype, Is);
+  if (int s = ensure_arena(ctx, L.total)) return s;
+  char* base = (char*)ctx->arena;
+  cudaStream_t st = (cudaStream_t)stream;
+
+  {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_ROUTE);
+    if (int s = route_into(ctx, w->gate, x, T, H, E, k, bf16, base, L, st)) return s;
+    ctx->launches += 3;
+  }
+  const int* counts = (const int*)(base + L.counts);
+  const int* offsets = (const int*)(base + L.offsets);
+  {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_GATHER);
+    RL_CUDA(ctx, rl::launch_gather(x, bf16, (const int*)(base + L.perm_pair), k, P, H, base + L.x_perm, st),
+            "gather");
+    ctx->launches += 1;
+  }
+
+  if (bf16) {
+    rl::TcGemmArgs g{};
+    g.w = w->gate_up_proj;
+    g.K = H;
+    g.rows_per_expert = 2 * I;
+    g.a1_offset = I;
+    g.m_step = 128;
+    g.m_tiles = I / 128;
+    g.b = base + L.x_perm;
+    g.P = P;
+    g.counts = counts;
+    g.offsets = offsets;
+    g.E = E;
+    g.swiglu = true;
+    g.h_out = (uint16_t*)(base + L.h_perm);
+    g.ld_out = I;
+    g.status = ctx->d_status;
+    {
+      PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
+      RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
+      ctx->launches += 1;
+    }
+    rl::TcGemmArgs d{};
+    d.w = w->down_proj;
+    d.K = I;
+    d.rows_per_expert = H;
+    d.a1_offset = 128;
+    d.m_step = 256;
+    d.m_tiles = H / 256;
+    d.b = base + L.h_perm;
+    d.P = P;
+    d.counts = counts;
+    d.offsets = offsets;
+    d.E = E;
+    d.swiglu = false;
+    d.y_out = (float*)(base + L.y_perm);
+    d.ld_out = H;
+    d.status = ctx->d_status;
+    {
+      PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
+      RL_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");
+      ctx->launches += 1;
+    }
+  } else {
+    float* proj = (float*)(base + L.proj);
+    rl::GroupedF32Args g{};
+    g.w = w->gate_up_proj;
+    g.K = H;
+    g.rows = 2 * I;
+    g.rows_per_expert = 2 * I;
+    g.row_offset = 0;
+    g.x = base + L.x_perm;
+    g.x_bf16 = false;
+    g.y = proj;
+    g.ldy = 2 * I;
+    g.y_col0 = 0;
+    g.counts = counts;
+    g.offsets = offsets;
+    g.E = E;
+    g.P = P;
+    g.round_w_bf16 = false;
+    {
+      PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
+      RL_CUDA(ctx, rl::launch_grouped_f32(g, st), "expert gate_up (f32)");
+      RL_CUDA(ctx, rl::launch_swiglu(proj, 2 * I, proj + I, 2 * I, base + L.h_perm, I, P, I, false, st),
+              "swiglu");
+      ctx->launches += 2;
+    }
+    rl::GroupedF32Args d = g;
+    d.w = w->down_proj;
+    d.K = I;
+    d.rows = H;
+    d.rows_per_expert = H;
+    d.x = base + L.h_perm;
+    d.y = (float*)(base + L.y_perm);
+    d.ldy = H;
+    {
+      PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
+      RL_CUDA(ctx, rl::launch_grouped_f32(d, st), "expert down (f32)");
+      ctx->launches += 1;
+    }
+  }
+
+  const float* shared_y = nullptr;
+  const float* shared_gate = nullptr;
+  if (shared) {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_SHARED);
+    ctx->launches += 5;
+    rl::GroupedF32Args s{};
+    s.K = H;
+    s.rows = Is;
+    s.rows_per_expert = Is;
+    s.row_offset = 0;
+    s.x = x;
+    s.x_bf16 = bf16;
+    s.ldy = Is;
+    s.counts = nullptr;
+    s.P = T;
+    s.E = 1;
+    s.round_w_bf16 = bf16;
+    s.w = w->shared_gate_proj;
+    s.y = (float*)(base + L.sh_g);
+    RL_CUDA(ctx, rl::launch_grouped_f32(s, st), "shared gate_proj");
+    s.w = w->shared_up_proj;
+    s.y = (float*)(base + L.sh_u);
+    RL_CUDA(ctx, rl::launch_grouped_f32(s, st), "shared up_proj");
+    RL_CUDA(ctx, rl::launch_swiglu((float*)(base + L.sh_g), Is, (float*)(base + L.sh_u), Is, base + L.sh_h,
+                                   Is, T, Is, bf16, st),
+            "shared swiglu");
+    rl::GroupedF32Args sd = s;
+    sd.w = w->shared_down_proj;
+    sd.K = Is;
+    sd.rows = H;
+    sd.rows_per_expert = H;
+    sd.x = base + L.sh_h;
+    sd.y = (float*)(base + L.sh_y);
+    sd.ldy = H;
+    RL_CUDA(ctx, rl::launch_grouped_f32(sd, st), "shared down_proj");
+    rl::GroupedF32Args sg = s;
+    sg.w = w->shared_expert_gate;
+    sg.rows = 1;
+    sg.rows_per_expert = 1;
+    sg.y = (float*)(base + L.sh_gate);
+    sg.ldy = 1;
+    sg.round_w_bf16 = false;
+    RL_CUDA(ctx, rl::launch_grouped_f32(sg, st), "shared expert gate");
+    shared_y = (const float*)(base + L.sh_y);
+    shared_gate = (const float*)(base + L.sh_gate);
+  }
+
+  {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_COMBINE);
+    RL_CUDA(ctx, rl::launch_combine((const float*)(base + L.y_perm), (const int*)(base + L.inv_pos),
+                                    (const int*)(base + L.topk_idx), (const float*)(base + L.topk_w), T, k, H,
+                                    shared_y, shared_gate, out, bf16, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st),
+            "combine");
+    ctx->launches += 1;
+  }
+  if (ctx->profiling) ctx->profiled_calls += 1;
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_profile_enable(riallm_ctx* ctx, int32_t enable) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  ctx->profiling = enable != 0;
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_profile_read(riallm_ctx* ctx, float* ms_per_phase, uint64_t* calls) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  float acc[RIALLM_NUM_PHASES] = {0};
+  int status = RIALLM_OK;
+  for (auto& pe : ctx->pending) {
+    float ms = 0.0f;
+    cudaError_t e = cudaEventSynchronize(pe.stop);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, pe.start, pe.stop);
+    if (e != cudaSuccess && status == RIALLM_OK) status = cuda_err(ctx, e, "profile event");
+    if (pe.phase >= 0 && pe.phase < RIALLM_NUM_PHASES) acc[pe.phase] += ms;
+    ctx->event_pool.push_back(pe.start);
+    ctx->event_pool.push_back(pe.stop);
+  }
+  ctx->pending.clear();
+  if (ms_per_phase)
+    for (int i = 0; i < RIALLM_NUM_PHASES; ++i) ms_per_phase[i] = acc[i];
+  if (calls) *calls = ctx->profiled_calls;
+  ctx->profiled_calls = 0;
+  return status;
+}
+
+uint64_t riallm_cuda_launch_count(const riallm_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,120 @@
+// internal.h -- declarations shared by the translation units of
+// libriallm_cuda. Not part of the public ABI (include/riallm_cuda.h is).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/riallm_cuda.h"
+
+struct riallm_ctx {
+  int device = 0;
+  int num_sms = 148;
+  std::string last_error;
+  // Scratch arena for one MoE block call: grown with cudaMalloc on demand,
+  // never shrunk, freed with the context.
+  void* arena = nullptr;
+  uint64_t arena_bytes = 0;
+  // Device status word written by kernels whose bounded waits expired.
+  int* d_status = nullptr;
+  // Kernel launches issued by this context.
+  uint64_t launches = 0;
+  // Phase profiling: event pairs recorded per call, summed on read.
+  bool profiling = false;
+  struct PhaseEvents {
+    int phase;
+    cudaEvent_t start, stop;
+  };
+  std::vector<PhaseEvents> pending;
+  std::vector<cudaEvent_t> event_pool;
+  uint64_t profiled_calls = 0;
+};
+
+namespace rl {
+
+// Offsets of the MoE scratch buffers inside one arena (all 1 KiB aligned).
+struct MoeLayout {
+  uint64_t wg, topk_idx, topk_w, counts, offsets, perm_pair, inv_pos;
+  uint64_t x_perm, h_perm, y_perm, proj;
+  uint64_t sh_g, sh_u, sh_h, sh_y, sh_gate;
+  uint64_t total;
+};
+MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int shared_I);
+
+cudaError_t launch_dequant(const riallm_qtensor& t, int mode, void* dst, int dst_dtype,
+                           int num_sms, cudaStream_t stream);
+cudaError_t launch_quantize(int qtype, const float* src, uint64_t n, uint8_t* data,
+                            float* scales, float* zeros, int num_sms, cudaStream_t stream);
+
+// Router (fixed-order fp32 dot products, own exp, stable top-k).
+cudaError_t launch_router(const void* x, bool x_bf16, const float* wg, int T, int H, int E, int k,
+                          int* topk_idx, float* topk_w, cudaStream_t stream);
+// Counting sort of the T*k (token, choice) pairs by expert.
+cudaError_t launch_permute(const int* topk_idx, int P, int E, int* counts, int* offsets,
+                           int* perm_pair, int* inv_pos, cudaStream_t stream);
+// Gathers token rows into expert-sorted pair order.
+cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int k, int P, int H,
+                          void* x_perm, cudaStream_t stream);
+// out[t] = sum over t's pairs in expert-ascending order of w * y_perm[pos]
+// (+ shared expert), optional residual add, cast to the activation dtype.
+cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* topk_idx,
+                           const float* topk_w, int T, int k, int H, const float* shared_y,
+                           const float* shared_gate, void* out, bool out_bf16, bool add_to_out,
+                           cudaStream_t stream);
+
+// Generic CUDA-core grouped GEMM with on-the-fly dequant (float32 path and
+// the shared expert): Y[pos, r] = sum_c X[pos, c] * W[row_base(e) + r, c].
+// X is float32 or bf16 [P, K]; Y float32 [P, ldy].
+struct GroupedF32Args {
+  riallm_qtensor w;
+  int K;
+  int rows;             // output rows per expert
+  int rows_per_expert;  // row stride between experts inside w
+  int row_offset;       // first weight row used inside an expert
+  const void* x;
+  bool x_bf16;
+  float* y;
+  int ldy;
+  int y_col0;
+  const int* counts;   // nullptr: a single group of P rows
+  const int* offsets;
+  int E;
+  int P;
+  bool round_w_bf16;
+};
+cudaError_t launch_grouped_f32(const GroupedF32Args& a, cudaStream_t stream);
+// h[pos, i] = silu(g[pos, i]) * u[pos, i] (optionally rounded to bf16).
+cudaError_t launch_swiglu(const float* g, int ldg, const float* u, int ldu, void* h, int ldh,
+                          int P, int I, bool h_bf16, cudaStream_t stream);
+
+// tcgen05 grouped expert GEMM with in-register dequant (bf16 activations).
+struct TcGemmArgs {
+  riallm_qtensor w;
+  int K;                // reduction length (H for gate_up, I for down)
+  int rows_per_expert;  // 2I (gate_up) or H (down)
+  int a1_offset;        // row offset of operand 1 inside a tile: I or 128
+  int m_step;           // rows per M tile step: 128 (gate_up) or 256 (down)
+  int m_tiles;          // I/128 or H/256
+  const void* b;        // bf16 [P, K] in pair order (x_perm or h_perm)
+  int P;
+  const int* counts;
+  const int* offsets;
+  int E;
+  bool swiglu;          // gate_up epilogue (h = silu(D0) * D1) vs down (y = D0 | D1)
+  uint16_t* h_out;      // [P, ld_out] bf16 when swiglu
+  float* y_out;         // [P, ld_out] f32 otherwise
+  int ld_out;
+  int* status;
+};
+cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream);
+
+// Driver entry point for cuTensorMapEncodeTiled (resolved at run time).
+CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                              uint64_t dim0, uint64_t dim1, uint64_t row_stride_bytes,
+                              uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle);
+
+}  // namespace rl

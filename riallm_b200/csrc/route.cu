@@ -1,0 +1,447 @@
+// route.cu -- router, token permutation, gather, combine, and the CUDA-core
+// grouped GEMM used by the float32 path and the shared expert.
+//
+// Router arithmetic is fixed so routing is reproducible bit for bit:
+//   logit[t,e] = xor-butterfly sum (offsets 16,8,4,2,1) of 32 lane partials;
+//     lane l accumulates, with fused multiply-adds, the 8-element chunks
+//     c = l, l+32, ... of x[t] . wg[e] in ascending order;
+//   softmax: max, own exp (Cody-Waite + degree-7 Taylor, fused), sequential
+//     sum over e, IEEE division;
+//   top-k: stable descending order (ties to the lower expert index), as
+//     candle's arg_sort_last_dim(false) in src/model.rs:764-767;
+//   renormalise by the sequential sum of the k picked probabilities
+//     (src/model.rs:768-770).
+#include "common.cuh"
+#include "internal.h"
+
+namespace rl {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// e^x: Cody & Waite argument reduction x = n ln2 + r with ln2 split into a
+// 16-bit head and a tail, degree-7 Taylor polynomial of e^r (|r| <= ln2/2,
+// truncation < 6e-9 relative) in fused Horner form, times 2^n. Inputs below
+// -87 return 0; the router only feeds x - max <= 0.
+__device__ __forceinline__ float own_expf(float x) {
+  if (x != x) return x;
+  if (x < -87.0f) return 0.0f;
+  if (x > 88.0f) return __int_as_float(0x7f800000);
+  const float t = __fmul_rn(x, 0x1.715476p+0f);
+  const float n = rintf(t);
+  float r = __fmaf_rn(-n, 0x1.62e4p-1f, x);
+  r = __fmaf_rn(-n, 0x1.7f7d1cp-20f, r);
+  float p = 0x1.a01a02p-13f;
+  p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+  p = __fmaf_rn(p, r, 0x1.111112p-7f);
+  p = __fmaf_rn(p, r, 0x1.555556p-5f);
+  p = __fmaf_rn(p, r, 0x1.555556p-3f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int ni = (int)n;
+  const float scale = __int_as_float((ni + 127) << 23);
+  return __fmul_rn(p, scale);
+}
+
+__device__ __forceinline__ void load_chunk8(const void* x, bool x_bf16, uint64_t off, float (&v)[8]) {
+  if (x_bf16) {
+    uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + off));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + off);
+    float4 a = __ldg(p), b = __ldg(p + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+// One warp per token. Shared memory: per warp E logits and E probabilities.
+__global__ void router_kernel(const void* __restrict__ x, int x_bf16, const float* __restrict__ wg,
+                              int T, int H, int E, int k, int* __restrict__ topk_idx,
+                              float* __restrict__ topk_w) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= T) return;
+  float* lg = sm + (size_t)warp * 2 * E;
+  float* pr = lg + E;
+  const int nchunk = H >> 3;
+  const uint64_t xrow = (uint64_t)t * H;
+  for (int e0 = 0; e0 < E; e0 += 8) {
+    const int ne = min(8, E - e0);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int c = lane; c < nchunk; c += 32) {
+      float xv[8];
+      load_chunk8(x, x_bf16 != 0, xrow + 8ull * c, xv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < ne) {
+          const float4* wp = reinterpret_cast<const float4*>(wg + (uint64_t)(e0 + j) * H + 8ull * c);
+          float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
+          float a = acc[j];
+          a = __fmaf_rn(xv[0], w0.x, a);
+          a = __fmaf_rn(xv[1], w0.y, a);
+          a = __fmaf_rn(xv[2], w0.z, a);
+          a = __fmaf_rn(xv[3], w0.w, a);
+          a = __fmaf_rn(xv[4], w1.x, a);
+          a = __fmaf_rn(xv[5], w1.y, a);
+          a = __fmaf_rn(xv[6], w1.z, a);
+          a = __fmaf_rn(xv[7], w1.w, a);
+          acc[j] = a;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j < ne) {
+        float v = acc[j];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(kFull, v, off));
+        if (lane == 0) lg[e0 + j] = v;
+      }
+    }
+  }
+  __syncwarp();
+  float m = __int_as_float(0xff800000);
+  for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
+  for (int e = lane; e < E; e += 32) pr[e] = own_expf(__fsub_rn(lg[e], m));
+  __syncwarp();
+  if (lane == 0) {
+    float s = 0.0f;
+    for (int e = 0; e < E; ++e) s = __fadd_rn(s, pr[e]);
+    for (int e = 0; e < E; ++e) pr[e] = __fdiv_rn(pr[e], s);
+    // Stable descending selection: strict > keeps the lower index on ties.
+    // lg[] is reused as the "taken" mark.
+    for (int e = 0; e < E; ++e) lg[e] = 0.0f;
+    int sel[16];
+    float ssum = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      int best = -1;
+      for (int e = 0; e < E; ++e) {
+        if (lg[e] != 0.0f) continue;
+        if (best < 0 || pr[e] > pr[best]) best = e;
+      }
+      lg[best] = 1.0f;
+      sel[j] = best;
+    }
+    for (int j = 0; j < k; ++j) ssum = __fadd_rn(ssum, pr[sel[j]]);
+    for (int j = 0; j < k; ++j) {
+      topk_idx[(uint64_t)t * k + j] = sel[j];
+      if (topk_w) topk_w[(uint64_t)t * k + j] = __fdiv_rn(pr[sel[j]], ssum);
+    }
+  }
+}
+
+cudaError_t launch_router(const void* x, bool x_bf16, const float* wg, int T, int H, int E, int k,
+                          int* topk_idx, float* topk_w, cudaStream_t stream) {
+  const int warps = 8;
+  const size_t smem = (size_t)warps * 2 * E * sizeof(float);
+  router_kernel<<<(T + warps - 1) / warps, warps * 32, smem, stream>>>(x, x_bf16 ? 1 : 0, wg, T, H,
+                                                                      E, k, topk_idx, topk_w);
+  return cudaGetLastError();
+}
+
+// One CTA of 1024 threads. Pass 1: per-warp expert histograms over
+// contiguous pair segments. Scan: offsets per expert and a base per
+// (warp, expert). Pass 2: each warp walks its segment in order, ranking
+// equal experts inside each 32-pair batch with match_any, so positions are
+// stable (pair order) inside every expert.
+constexpr int kPermMaxE = 256;
+__global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ topk_idx, int P, int E,
+                                                       int* __restrict__ counts, int* __restrict__ offsets,
+                                                       int* __restrict__ perm_pair,
+                                                       int* __restrict__ inv_pos) {
+  __shared__ int hist[32][kPermMaxE + 1];
+  __shared__ int off_s[kPermMaxE + 1];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < 32 * (kPermMaxE + 1); i += blockDim.x) (&hist[0][0])[i] = 0;
+  __syncthreads();
+  const int per = (P + 31) / 32;
+  const int p0 = min(P, warp * per), p1 = min(P, p0 + per);
+  for (int p = p0 + lane; p < p1; p += 32) atomicAdd(&hist[warp][topk_idx[p]], 1);
+  __syncthreads();
+  if (tid < E) {
+    int c = 0;
+    for (int w = 0; w < 32; ++w) c += hist[w][tid];
+    off_s[tid + 1] = c;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    off_s[0] = 0;
+    for (int e = 0; e < E; ++e) off_s[e + 1] += off_s[e];
+  }
+  __syncthreads();
+  if (tid < E) {
+    int b = off_s[tid];
+    counts[tid] = off_s[tid + 1] - off_s[tid];
+    for (int w = 0; w < 32; ++w) {
+      const int h = hist[w][tid];
+      hist[w][tid] = b;
+      b += h;
+    }
+  }
+  if (tid <= E) offsets[tid] = off_s[tid];
+  __syncthreads();
+  for (int base = p0; base < p1; base += 32) {
+    const int p = base + lane;
+    const bool valid = p < p1;
+    const unsigned act = __ballot_sync(kFull, valid);
+    if (valid) {
+      const int e = topk_idx[p];
+      const unsigned peers = __match_any_sync(act, e);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      const int pos = hist[warp][e] + rank;
+      perm_pair[pos] = p;
+      if (inv_pos) inv_pos[p] = pos;
+      __syncwarp(act);
+      if (rank == 0) hist[warp][e] += __popc(peers);
+    }
+    __syncwarp();
+  }
+}
+
+cudaError_t launch_permute(const int* topk_idx, int P, int E, int* counts, int* offsets,
+                           int* perm_pair, int* inv_pos, cudaStream_t stream) {
+  permute_kernel<<<1, 1024, 0, stream>>>(topk_idx, P, E, counts, offsets, perm_pair, inv_pos);
+  return cudaGetLastError();
+}
+
+// One warp per pair row; 16-byte copies.
+__global__ void gather_kernel(const void* __restrict__ x, int x_bf16, const int* __restrict__ perm_pair,
+                              int k, int P, int H, void* __restrict__ x_perm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (row >= P) return;
+  const int t = perm_pair[row] / k;
+  const int esz = x_bf16 ? 2 : 4;
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(x) + (uint64_t)t * H * esz);
+  uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(x_perm) + (uint64_t)row * H * esz);
+  const int n16 = H * esz / 16;
+  for (int i = lane; i < n16; i += 32) dst[i] = __ldg(src + i);
+}
+
+cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int k, int P, int H,
+                          void* x_perm, cudaStream_t stream) {
+  if (P == 0) return cudaSuccess;
+  const int warps = 8;
+  gather_kernel<<<(P + warps - 1) / warps, warps * 32, 0, stream>>>(x, x_bf16 ? 1 : 0, perm_pair, k,
+                                                                    P, H, x_perm);
+  return cudaGetLastError();
+}
+
+// One CTA per token; 4 columns per thread per step. The token's pairs are
+// visited in expert-ascending order (the reference's index_add order,
+// src/model.rs:794-811): acc = acc + y * w, one rounding each, from 0.
+__global__ void combine_kernel(const float* __restrict__ y_perm, const int* __restrict__ inv_pos,
+                               const int* __restrict__ topk_idx, const float* __restrict__ topk_w,
+                               int k, int H, const float* __restrict__ shared_y,
+                               const float* __restrict__ shared_gate, void* out, int out_bf16,
+                               int add_to_out) {
+  const int t = blockIdx.x;
+  int ord[16];
+  int exp_id[16];
+  for (int j = 0; j < k; ++j) {
+    exp_id[j] = topk_idx[(uint64_t)t * k + j];
+    ord[j] = j;
+  }
+  for (int a = 1; a < k; ++a) {
+    int v = ord[a];
+    int b = a - 1;
+    while (b >= 0 && exp_id[ord[b]] > exp_id[v]) {
+      ord[b + 1] = ord[b];
+      --b;
+    }
+    ord[b + 1] = v;
+  }
+  float gsig = 0.0f;
+  if (shared_y) gsig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-shared_gate[t])));
+  for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int jj = 0; jj < k; ++jj) {
+      const int j = ord[jj];
+      const int pos = inv_pos[(uint64_t)t * k + j];
+      const float w = topk_w[(uint64_t)t * k + j];
+      const float4 y = *reinterpret_cast<const float4*>(y_perm + (uint64_t)pos * H + h);
+      a0 = __fadd_rn(a0, __fmul_rn(y.x, w));
+      a1 = __fadd_rn(a1, __fmul_rn(y.y, w));
+      a2 = __fadd_rn(a2, __fmul_rn(y.z, w));
+      a3 = __fadd_rn(a3, __fmul_rn(y.w, w));
+    }
+    if (shared_y) {
+      const float4 s = *reinterpret_cast<const float4*>(shared_y + (uint64_t)t * H + h);
+      a0 = __fadd_rn(a0, __fmul_rn(s.x, gsig));
+      a1 = __fadd_rn(a1, __fmul_rn(s.y, gsig));
+      a2 = __fadd_rn(a2, __fmul_rn(s.z, gsig));
+      a3 = __fadd_rn(a3, __fmul_rn(s.w, gsig));
+    }
+    const uint64_t o = (uint64_t)t * H + h;
+    if (out_bf16) {
+      __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(out);
+      if (add_to_out) {
+        a0 = __fadd_rn(a0, __bfloat162float(ob[o]));
+        a1 = __fadd_rn(a1, __bfloat162float(ob[o + 1]));
+        a2 = __fadd_rn(a2, __bfloat162float(ob[o + 2]));
+        a3 = __fadd_rn(a3, __bfloat162float(ob[o + 3]));
+      }
+      uint2 pk;
+      pk.x = pack_bf16x2(a0, a1);
+      pk.y = pack_bf16x2(a2, a3);
+      *reinterpret_cast<uint2*>(ob + o) = pk;
+    } else {
+      float* of = reinterpret_cast<float*>(out);
+      if (add_to_out) {
+        a0 = __fadd_rn(a0, of[o]);
+        a1 = __fadd_rn(a1, of[o + 1]);
+        a2 = __fadd_rn(a2, of[o + 2]);
+        a3 = __fadd_rn(a3, of[o + 3]);
+      }
+      *reinterpret_cast<float4*>(of + o) = make_float4(a0, a1, a2, a3);
+    }
+  }
+}
+
+cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* topk_idx,
+                           const float* topk_w, int T, int k, int H, const float* shared_y,
+                           const float* shared_gate, void* out, bool out_bf16, bool add_to_out,
+                           cudaStream_t stream) {
+  if (T == 0) return cudaSuccess;
+  const int threads = H >= 1024 ? 256 : 128;
+  combine_kernel<<<T, threads, 0, stream>>>(y_perm, inv_pos, topk_idx, topk_w, k, H, shared_y,
+                                            shared_gate, out, out_bf16 ? 1 : 0, add_to_out ? 1 : 0);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------- CUDA-core grouped GEMM
+
+// Element e of a tensor in the reference layout, as float32 (same closed
+// form as the dequant kernels: NF4 block (e+1)/bs, 8-bit block e/bs).
+__device__ __forceinline__ float weight_elem(const riallm_qtensor& w, uint64_t e) {
+  if (w.qtype == RIALLM_COMPRESSION_NONE) return __ldg(reinterpret_cast<const float*>(w.data) + e);
+  const uint8_t* d = reinterpret_cast<const uint8_t*>(w.data);
+  uint32_t code;
+  uint64_t b;
+  if (w.qtype == RIALLM_COMPRESSION_FOUR_BIT) {
+    const uint8_t byte = __ldg(d + (e >> 1));
+    code = (e & 1) ? (byte >> 4) & 15u : byte & 15u;
+    b = (e + 1) / (uint64_t)w.block_size;
+  } else {
+    code = __ldg(d + e);
+    b = e / (uint64_t)w.block_size;
+  }
+  const float scale = b < w.n_scales ? __ldg(w.scales + b) : 1.0f;
+  const float zero = b < w.n_zero_points ? __ldg(w.zero_points + b) : 0.0f;
+  return __fmul_rn(__fsub_rn((float)code, zero), scale);
+}
+
+// Tile: 64 weight rows x 16 pairs, K in steps of 32. Block (x = row tile,
+// y = enumerated (expert, pair tile)). 256 threads: thread (r, g) owns row
+// r and pairs 4g..4g+3.
+constexpr int kGR = 64, kGN = 16, kGK = 32;
+__global__ void __launch_bounds__(256) grouped_f32_kernel(GroupedF32Args a) {
+  __shared__ float ws[kGR][kGK + 1];
+  __shared__ float xs[kGN][kGK + 1];
+  // Find this block's (expert, pair tile).
+  int e = 0, n0 = 0, cnt = a.P, off = 0;
+  int y = blockIdx.y;
+  if (a.counts) {
+    bool found = false;
+    for (e = 0; e < a.E; ++e) {
+      const int c = a.counts[e];
+      const int nt = (c + kGN - 1) / kGN;
+      if (y < nt) {
+        found = true;
+        break;
+      }
+      y -= nt;
+    }
+    if (!found) return;
+    cnt = a.counts[e];
+    off = a.offsets[e];
+  } else {
+    if (y * kGN >= a.P) return;
+  }
+  n0 = y * kGN;
+  const int r0 = blockIdx.x * kGR;
+  const int tid = threadIdx.x;
+  const int r = tid & 63, g = tid >> 6;
+  const uint64_t wrow0 = (uint64_t)e * a.rows_per_expert + a.row_offset + r0;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < a.K; k0 += kGK) {
+    for (int i = tid; i < kGR * kGK; i += 256) {
+      const int rr = i / kGK, kk = i % kGK;
+      float v = 0.0f;
+      if (r0 + rr < a.rows && k0 + kk < a.K) {
+        v = weight_elem(a.w, (wrow0 + rr) * (uint64_t)a.K + k0 + kk);
+        if (a.round_w_bf16) v = __bfloat162float(__float2bfloat16_rn(v));
+      }
+      ws[rr][kk] = v;
+    }
+    for (int i = tid; i < kGN * kGK; i += 256) {
+      const int nn = i / kGK, kk = i % kGK;
+      float v = 0.0f;
+      if (n0 + nn < cnt && k0 + kk < a.K) {
+        const uint64_t idx = (uint64_t)(off + n0 + nn) * a.K + k0 + kk;
+        v = a.x_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(a.x)[idx])
+                     : reinterpret_cast<const float*>(a.x)[idx];
+      }
+      xs[nn][kk] = v;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kGK; ++kk) {
+      const float wv = ws[r][kk];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = __fmaf_rn(wv, xs[4 * g + j][kk], acc[j]);
+    }
+    __syncthreads();
+  }
+  if (r0 + r < a.rows) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + 4 * g + j;
+      if (n < cnt) a.y[(uint64_t)(off + n) * a.ldy + a.y_col0 + r0 + r] = acc[j];
+    }
+  }
+}
+
+cudaError_t launch_grouped_f32(const GroupedF32Args& a, cudaStream_t stream) {
+  if (a.P == 0) return cudaSuccess;
+  dim3 grid((a.rows + kGR - 1) / kGR, (a.P + kGN - 1) / kGN + (a.counts ? a.E : 0));
+  grouped_f32_kernel<<<grid, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+__global__ void swiglu_kernel(const float* __restrict__ g, int ldg, const float* __restrict__ u, int ldu,
+                              void* __restrict__ h, int ldh, int P, int I, int h_bf16) {
+  const uint64_t n = (uint64_t)P * I;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t p = i / I, c = i % I;
+    const float gv = g[p * ldg + c];
+    const float uv = u[p * ldu + c];
+    const float hv = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+    if (h_bf16)
+      reinterpret_cast<__nv_bfloat16*>(h)[p * ldh + c] = __float2bfloat16_rn(hv);
+    else
+      reinterpret_cast<float*>(h)[p * ldh + c] = hv;
+  }
+}
+
+cudaError_t launch_swiglu(const float* g, int ldg, const float* u, int ldu, void* h, int ldh, int P,
+                          int I, bool h_bf16, cudaStream_t stream) {
+  if (P == 0) return cudaSuccess;
+  const uint64_t n = (uint64_t)P * I;
+  const uint64_t nb = (n + 255) / 256;
+  const int blocks = (int)(nb < 148ull * 16 ? nb : 148ull * 16);
+  swiglu_kernel<<<blocks, 256, 0, stream>>>(g, ldg, u, ldu, h, ldh, P, I, h_bf16 ? 1 : 0);
+  return cudaGetLastError();
+}
+
+}  // namespace rl

@@ -1,0 +1,172 @@
+"""GPU parity of the whole MoE block (src/model.rs:751-818) against the
+oracle and the golden fixtures.
+
+Tolerances (max |gpu - ref| / max |ref|): 2e-2 for bf16 activations and
+1e-4 for float32 activations. Routing (indices, counts) must be bit-exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import device_q, load_golden, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = {True: 2e-2, False: 1e-4}
+
+
+def to_dev_x(x, bf16):
+    if bf16:
+        return torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).cuda().view(torch.bfloat16)
+    return torch.from_numpy(np.ascontiguousarray(x)).cuda()
+
+
+def dev_tensors(rb, w):
+    def q(t):
+        if t is None:
+            return None
+        return rb.QuantizedTensor(torch.from_numpy(t.data).cuda(), (t.numel,), rb.CompressionType(t.qtype),
+                                  torch.from_numpy(t.scales).cuda(), torch.from_numpy(t.zero_points).cuda(),
+                                  t.block_size)
+    d = {"mlp.gate.weight": q(w.gate), "mlp.experts.gate_up_proj": q(w.gate_up_proj),
+         "mlp.experts.down_proj": q(w.down_proj)}
+    if w.shared_gate_proj is not None:
+        d["mlp.shared_expert.gate_proj.weight"] = q(w.shared_gate_proj)
+        d["mlp.shared_expert.up_proj.weight"] = q(w.shared_up_proj)
+        d["mlp.shared_expert.down_proj.weight"] = q(w.shared_down_proj)
+        d["mlp.shared_expert_gate.weight"] = q(w.shared_expert_gate)
+        d["mlp.shared_expert.gate_proj.weight"].shape = (w.shared_intermediate, w.shared_gate_proj.numel // w.shared_intermediate)
+    return d
+
+
+def set_shapes(d, H, I, E):
+    d["mlp.gate.weight"].shape = (E, H)
+    d["mlp.experts.gate_up_proj"].shape = (E, 2 * I, H)
+    d["mlp.experts.down_proj"].shape = (E, H, I)
+    return d
+
+
+@pytest.mark.parametrize("name", ["moe_nf4_bf16", "moe_int8_bf16", "moe_nf4_f32",
+                                  "moe_nf4_bf16_k4_e8", "moe_nf4_bf16_shared"])
+def test_golden_moe(rb, name):
+    g = load_golden(name + ".npz")
+    H, I, E, k, T, qt, bf16, shared_I = [int(v) for v in g["dims"]]
+    d = {"mlp.gate.weight": device_q(rb, g, "gate"),
+         "mlp.experts.gate_up_proj": device_q(rb, g, "gate_up_proj"),
+         "mlp.experts.down_proj": device_q(rb, g, "down_proj")}
+    if shared_I:
+        for n, key in [("shared_gate_proj", "mlp.shared_expert.gate_proj.weight"),
+                       ("shared_up_proj", "mlp.shared_expert.up_proj.weight"),
+                       ("shared_down_proj", "mlp.shared_expert.down_proj.weight"),
+                       ("shared_expert_gate", "mlp.shared_expert_gate.weight")]:
+            d[key] = device_q(rb, g, n)
+        d["mlp.shared_expert.gate_proj.weight"].shape = (shared_I, H)
+    set_shapes(d, H, I, E)
+    x = to_dev_x(g["x"], bool(bf16))
+    out = rb.apply_moe(d, x, k, E)
+    idx, *_ = rb.route(d["mlp.gate.weight"], x, k, E)
+    torch.cuda.synchronize()
+    assert np.array_equal(idx.cpu().numpy(), g["idx"])
+    err = rel_err(out.float().cpu().numpy(), g["out"])
+    assert err < TOL[bool(bf16)], err
+
+
+CASES = [
+    # T, H, I, E, k, qtype, bf16
+    (1, 256, 256, 8, 2, 1, True),
+    (3, 512, 256, 8, 2, 2, True),
+    (17, 256, 512, 4, 1, 1, True),
+    (64, 512, 512, 8, 2, 1, True),
+    (130, 256, 256, 2, 2, 1, True),    # 130 pairs per expert: two N tiles (128 + 16)
+    (300, 256, 256, 4, 2, 2, True),    # N tile widths 128/64/32/16 across experts
+    (9, 256, 256, 8, 2, 1, False),
+    (40, 512, 256, 8, 4, 2, False),
+]
+
+
+@pytest.mark.parametrize("T,H,I,E,k,qt,bf16", CASES)
+def test_moe_random_vs_oracle(rb, oracle_lib, T, H, I, E, k, qt, bf16):
+    O = oracle_lib
+    w, _ = O.synthetic_layer(H, I, E, qt, seed=T * 31 + H + E)
+    x = O.synthetic_x(T, H, seed=T + 5, bf16=bf16)
+    ref, idx_ref, _, counts_ref = O.moe_forward(w, x, T, H, I, E, k)
+    d = set_shapes(dev_tensors(rb, w), H, I, E)
+    xt = to_dev_x(x, bf16)
+    out = rb.apply_moe(d, xt, k, E)
+    idx, _, counts, *_ = rb.route(d["mlp.gate.weight"], xt, k, E)
+    torch.cuda.synchronize()
+    assert np.array_equal(idx.cpu().numpy(), idx_ref)
+    assert np.array_equal(counts.cpu().numpy(), counts_ref)
+    err = rel_err(out.float().cpu().numpy(), ref)
+    assert err < TOL[bf16], err
+
+
+def test_add_to_out_and_empty(rb, oracle_lib):
+    O = oracle_lib
+    H, I, E, k, T = 256, 256, 4, 2, 6
+    w, _ = O.synthetic_layer(H, I, E, 1, seed=77)
+    x = O.synthetic_x(T, H, seed=78)
+    ref, *_ = O.moe_forward(w, x, T, H, I, E, k)
+    d = set_shapes(dev_tensors(rb, w), H, I, E)
+    xt = to_dev_x(x, True)
+    resid = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    out = resid.clone()
+    rb.apply_moe(d, xt, k, E, out=out, add_to_out=True)
+    want = resid.float().cpu().numpy() + ref
+    assert rel_err(out.float().cpu().numpy(), want) < 2e-2
+    empty = rb.apply_moe(d, xt[:0], k, E)
+    assert empty.shape == (0, H)
+
+
+def test_missing_tensor_and_bad_config(rb, oracle_lib):
+    O = oracle_lib
+    w, _ = O.synthetic_layer(256, 256, 4, 1, seed=1)
+    d = set_shapes(dev_tensors(rb, w), 256, 256, 4)
+    x = to_dev_x(O.synthetic_x(2, 256, seed=2), True)
+    bad = dict(d)
+    del bad["mlp.experts.down_proj"]
+    with pytest.raises(rb.ModelLoadingError, match="Tensor not found: mlp.experts.down_proj"):
+        rb.apply_moe(bad, x, 2, 4)
+    with pytest.raises(rb.ConfigError):
+        rb.apply_moe(d, x, 5, 4)  # k > E
+
+
+def torch_reference(rb, d, x, k, E, H, I):
+    """fp32 torch reference from the bit-exact dequantized weights (bf16-rounded
+    as the bf16 path computes) for the experts the router picked."""
+    idx, tw, *_ = rb.route(d["mlp.gate.weight"], x, k, E)
+    gu = d["mlp.experts.gate_up_proj"]
+    dn = d["mlp.experts.down_proj"]
+    xf = x.float()
+    out = torch.zeros(x.shape[0], H, device="cuda")
+    full_gu = gu.dequantize(torch.bfloat16).view(E, 2 * I, H)
+    full_dn = dn.dequantize(torch.bfloat16).view(E, H, I)
+    for e in range(E):
+        rows, slot = torch.nonzero(idx == e, as_tuple=True)
+        if rows.numel() == 0:
+            continue
+        p = xf[rows] @ full_gu[e].float().t()
+        h = (torch.nn.functional.silu(p[:, :I]) * p[:, I:]).to(torch.bfloat16).float()
+        y = h @ full_dn[e].float().t()
+        out.index_add_(0, rows, y * tw[rows, slot][:, None])
+    return out
+
+
+@pytest.mark.parametrize("T", [1, 64, 4096])
+def test_mixtral_shape_vs_torch_fp32(rb, T):
+    """Mixtral-8x7B-shaped block (H 4096, I 14336, E 8, top-2, NF4 from
+    N(0, 0.02) seed 2) against a float32 torch reference."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    H, I, E, k = 4096, 14336, 8, 2
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    d = {}
+    for name, shape in [("mlp.gate.weight", (E, H)), ("mlp.experts.gate_up_proj", (E, 2 * I, H)),
+                        ("mlp.experts.down_proj", (E, H, I))]:
+        w = torch.empty(shape, device="cuda").normal_(0.0, 0.02, generator=gen)
+        d[name] = rb.quantize_tensor(w, rb.CompressionType.FourBit)
+        del w
+    x = torch.empty(T, H, device="cuda").normal_(0, 1, generator=gen).to(torch.bfloat16)
+    out = rb.apply_moe(d, x, k, E)
+    ref = torch_reference(rb, d, x, k, E, H, I)
+    err = ((out.float() - ref).abs().max() / ref.abs().max()).item()
+    assert err < 2e-2, err

@@ -1,0 +1,60 @@
+"""GPU parity of the router and bucketing (src/model.rs:762-789): top-k
+indices, renormalised weights, per-expert counts, offsets and permutation
+order bit-exact against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+
+def test_router_golden_bit_exact(rb):
+    g = load_golden("router.npz")
+    for tag in [k[2:] for k in g if k.startswith("x_")]:
+        E = int(tag.split("_E")[1].split("_")[0])
+        k = int(tag.split("_k")[1])
+        x = torch.from_numpy(g[f"x_{tag}"].view(np.int16)).cuda().view(torch.bfloat16)
+        wg = torch.from_numpy(g[f"wg_{tag}"]).cuda()
+        idx, w, counts, offsets, perm = rb.route(wg, x, k, E)
+        torch.cuda.synchronize()
+        assert np.array_equal(idx.cpu().numpy(), g[f"idx_{tag}"]), tag
+        assert np.array_equal(w.cpu().numpy().view(np.uint32), g[f"w_{tag}"].view(np.uint32)), tag
+        assert np.array_equal(counts.cpu().numpy(), g[f"counts_{tag}"]), tag
+        assert np.array_equal(offsets.cpu().numpy(), g[f"offsets_{tag}"]), tag
+        assert np.array_equal(perm.cpu().numpy(), g[f"perm_{tag}"]), tag
+
+
+@pytest.mark.parametrize("T,H,E,k,qt,bf16", [
+    (64, 4096, 8, 2, 1, True),      # Mixtral-8x7B router, NF4-quantized (32768 >= 4096)
+    (1, 4096, 8, 2, 1, True),
+    (333, 2048, 128, 8, 2, True),   # fine-grained 128-expert top-8, 8-bit router
+    (4096, 1024, 8, 2, 1, True),
+    (50, 512, 16, 4, 1, False),     # float32 activations
+])
+def test_router_random_bit_exact(rb, oracle_lib, T, H, E, k, qt, bf16):
+    O = oracle_lib
+    rng = np.random.default_rng(T * 7 + E)
+    wg = rng.normal(0, 0.02, (E, H)).astype(np.float32)
+    qwg = O.quantize(wg, qt)
+    x = O.synthetic_x(T, H, T + 1, bf16=bf16)
+    _, _, idx_ref, w_ref = O.router(x, O.dequantize(qwg).reshape(E, H), k)
+    counts_ref, offsets_ref, perm_ref = O.bucket(idx_ref, E)
+    dev = rb.QuantizedTensor(torch.from_numpy(qwg.data).cuda(), (E, H), rb.CompressionType(qt),
+                             torch.from_numpy(qwg.scales).cuda(), torch.from_numpy(qwg.zero_points).cuda(),
+                             qwg.block_size)
+    xt = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16) if bf16 else torch.from_numpy(x).cuda()
+    idx, w, counts, offsets, perm = rb.route(dev, xt, k, E)
+    assert np.array_equal(idx.cpu().numpy(), idx_ref)
+    assert np.array_equal(w.cpu().numpy().view(np.uint32), w_ref.view(np.uint32))
+    assert np.array_equal(counts.cpu().numpy(), counts_ref)
+    assert np.array_equal(offsets.cpu().numpy(), offsets_ref)
+    assert np.array_equal(perm.cpu().numpy(), perm_ref)
+
+
+def test_router_ties_lower_index(rb):
+    x = torch.ones(3, 256, device="cuda", dtype=torch.bfloat16)
+    wg = torch.zeros(8, 256, device="cuda")
+    idx, w, *_ = rb.route(wg, x, 3, 8)
+    assert idx.cpu().tolist() == [[0, 1, 2]] * 3
