@@ -1,0 +1,465 @@
+#!/usr/bin/env python3
+"""bench.py -- MoE-layer tokens/s of the Mixtral-8x7B-shaped NF4 MoE block on B200.
+
+Workload (the isolated-block configuration): hidden 4096, 8 experts, top-2,
+SwiGLU intermediate 14336, weights N(0, 0.02) seed 2 quantized to NF4 with
+riallm's block format (0.625 B/weight, 880.8 MB for the layer), bf16
+activations N(0, 1). One step = one MoE block forward over one batch of
+tokens (default: a decode batch of 64). The weights are larger than the
+126 MB L2, so every step streams them from HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0. Multi-GPU (torchrun, one rank per GPU): each
+rank runs an independent replica of the block on its own batch (weak
+scaling, no collective on the data path); value is the total tokens of all
+ranks over the slowest rank's device time.
+
+--impl reference times the oracle's CPU port of riallm's MoE block
+(oracle/riallm_oracle.c, all host threads) on the same workload; the Rust
+reference itself cannot be built here.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I, E, TOP_K = 4096, 14336, 8, 2
+NF4_BYTES_PER_WEIGHT = 0.5 + 8.0 / 64.0          # codes + f32 scale and zero per 64
+WEIGHTS_PER_EXPERT = 3 * H * I                    # gate, up, down
+BYTES_PER_EXPERT = int(WEIGHTS_PER_EXPERT * NF4_BYTES_PER_WEIGHT)  # 110,100,480
+METRIC = "MoE-layer tokens/s & Mixtral-8x7B NF4 decode tok/s at 1/2/4/8 B200; % HBM peak"
+SWEEP_T = (1, 8, 32, 64, 4096)
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+            0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+            0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+            0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a thread."""
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        self._dev = device_index
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nv:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        if not self._nv or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        reasons = [name for bit, name in _REASONS.items() if self.reasons & bit and bit != 0x1]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------ distributed
+
+def dist_setup():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ----------------------------------------------------------- reference arm
+
+def run_reference(args, rank, world):
+    """Times the CPU port of riallm's MoE block (the oracle) on host cores."""
+    if rank != 0:
+        return 0
+    import numpy as np
+    from oracle import oracle as O
+
+    O.build()
+    t0 = time.time()
+    rng = np.random.default_rng(2)
+    layer = {}
+    for name, shape in (("gate", (E, H)), ("gate_up_proj", (E, 2 * I, H)), ("down_proj", (E, H, I))):
+        a = rng.standard_normal(size=shape, dtype=np.float32)
+        a *= np.float32(0.02)
+        layer[name] = O.quantize(a, O.FOUR_BIT)
+        del a
+    w = O.MoeWeights(layer["gate"], layer["gate_up_proj"], layer["down_proj"])
+    x = O.synthetic_x(args.tokens, H, seed=3, bf16=True)
+    setup_s = time.time() - t0
+    threads = os.cpu_count() or 1
+
+    # Size each step's sample so the whole run stays within a few minutes.
+    t1 = time.perf_counter()
+    O.moe_forward(w, x[:1], 1, H, I, E, TOP_K, n_threads=threads)
+    one_token_s = time.perf_counter() - t1
+    budget_s = 150.0
+    n_calls = args.warmup + args.steps
+    sample_tokens = args.tokens
+    est = n_calls * one_token_s * sample_tokens * 0.6  # tokens share dequantized rows
+    if est > budget_s:
+        sample_tokens = max(1, int(args.tokens * budget_s / est))
+    xs = x[:sample_tokens]
+    for _ in range(args.warmup):
+        O.moe_forward(w, xs, sample_tokens, H, I, E, TOP_K, n_threads=threads)
+    t2 = time.perf_counter()
+    for _ in range(args.steps):
+        O.moe_forward(w, xs, sample_tokens, H, I, E, TOP_K, n_threads=threads)
+    el = time.perf_counter() - t2
+    value = sample_tokens * args.steps / el
+    sample = (f"{sample_tokens} of the {args.tokens}-token decode batch per step, full 8-expert "
+              f"NF4 Mixtral block, fp32 oracle port, {threads} threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * el / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: N(0,0.02) weights (numpy seed 2) NF4-quantized; N(0,1) bf16 activations",
+        "config": config_dict(args, world),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "setup_s": round(setup_s, 1),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(args, world):
+    return {"workload": f"mixtral8x7b_moe_block_nf4_decode_T{args.tokens}",
+            "hidden": H, "intermediate": I, "experts": E, "top_k": TOP_K,
+            "tokens_per_step_per_gpu": args.tokens, "compression": "FourBit (riallm NF4 layout)",
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2_policy": "inputs larger than L2 (880.8 MB of NF4 weights per step vs 126 MB L2)"}
+
+
+# ------------------------------------------------------------------ ours
+
+def make_layer(rb, torch, device, seed=2):
+    """Seeded N(0, 0.02) weights quantized to NF4 in riallm's layout. Each
+    tensor is generated and quantized one expert slice at a time into the
+    full tensor's buffers (64-element blocks never straddle experts, so the
+    bytes, scales and zero points equal those of quantizing the whole tensor
+    at once); this keeps the device footprint near the 0.9 GB of NF4 data."""
+    import ctypes as C
+    gen = torch.Generator(device=device).manual_seed(seed)
+    L = rb.lib()
+    ctx = rb.Context.get(device.index or 0)
+    d = {}
+    for name, shape in (("mlp.gate.weight", (E, H)), ("mlp.experts.gate_up_proj", (E, 2 * I, H)),
+                        ("mlp.experts.down_proj", (E, H, I))):
+        numel = 1
+        for v in shape:
+            numel *= v
+        data = torch.empty(numel // 2, dtype=torch.uint8, device=device)
+        scales = torch.empty(numel // 64, dtype=torch.float32, device=device)
+        zeros = torch.empty(numel // 64, dtype=torch.float32, device=device)
+        chunk = numel // shape[0] if len(shape) == 3 else numel
+        for c0 in range(0, numel, chunk):
+            w = torch.empty(chunk, device=device).normal_(0.0, 0.02, generator=gen)
+            ctx.check(L.riallm_cuda_quantize(ctx.ptr, 1, w.data_ptr(), chunk, data.data_ptr() + c0 // 2,
+                                             scales.data_ptr() + 4 * (c0 // 64), zeros.data_ptr() + 4 * (c0 // 64),
+                                             torch.cuda.current_stream().cuda_stream))
+            del w
+        d[name] = rb.QuantizedTensor(data, shape, rb.CompressionType.FourBit, scales, zeros, 64)
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return d
+
+
+class Block:
+    """One MoE block call through the C ABI with fixed buffers (so it can be
+    captured in a CUDA graph)."""
+
+    def __init__(self, rb, torch, d, T, device):
+        self.rb, self.torch = rb, torch
+        self.ctx = rb.Context.get(device.index or 0)
+        self.w, self.keep, _ = rb._weights(d)
+        gen = torch.Generator(device=device).manual_seed(1000 + T)
+        self.x = torch.empty(T, H, device=device).normal_(0, 1, generator=gen).to(torch.bfloat16)
+        self.out = torch.empty_like(self.x)
+        self.T = T
+        self.ctx.reserve(T, H, I, E, TOP_K, torch.bfloat16)
+
+    def __call__(self, stream_ptr=None):
+        L = self.rb.lib()
+        st = stream_ptr if stream_ptr is not None else self.torch.cuda.current_stream().cuda_stream
+        rc = L.riallm_cuda_moe_forward(self.ctx.ptr, ctypes.byref(self.w), self.x.data_ptr(),
+                                       self.out.data_ptr(), self.T, H, I, E, TOP_K, 1, 0, st)
+        if rc:
+            self.ctx.check(rc)
+
+    def distinct_experts(self):
+        idx, _, counts, _, _ = self.rb.route(self.keep[0], self.x, TOP_K, E)
+        return int((counts > 0).sum().item())
+
+
+def expert_bytes(T, U):
+    """Algorithmic bytes of the two expert-GEMM launches of one step."""
+    P = T * TOP_K
+    return U * BYTES_PER_EXPERT + P * H * 2 + 2 * P * I * 2 + P * H * 4
+
+
+def expert_flops(T):
+    return 2.0 * T * TOP_K * 3 * H * I
+
+
+def timed(torch, fn, steps, warmup, dist, world):
+    for _ in range(warmup):
+        fn()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def phase_profile(torch, blk, steps):
+    """Per-phase device time from CUDA events recorded by the library on the
+    launching stream. A sleep kernel queued first keeps the GPU busy while the
+    host enqueues every step, so no host gap lands inside an event pair."""
+    torch.cuda.synchronize()
+    blk.ctx.profile(True)
+    torch.cuda._sleep(int(2e8))
+    for _ in range(steps):
+        blk()
+    torch.cuda.synchronize()
+    blk.ctx.profile(False)
+    ph, calls = blk.ctx.profile_read()
+    return {k: v / max(calls, 1) for k, v in ph.items()}, calls
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    import riallm_b200 as rb
+
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    hbm_peak, bf16_peak, bf16_sust, peak_src = load_peaks()
+
+    d = make_layer(rb, torch, device)
+    blk = Block(rb, torch, d, args.tokens, device)
+    U = blk.distinct_experts()
+
+    # Capture one step in a CUDA graph (after a warm-up that sizes the arena).
+    for _ in range(3):
+        blk()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            blk(s.cuda_stream)
+    torch.cuda.synchronize()
+
+    launches0 = blk.ctx.launch_count()
+    with ClockSampler(local) as clk:
+        ms = timed(torch, g.replay, args.steps, args.warmup, dist, world)
+    per_step_launches = (blk.ctx.launch_count() - launches0)  # captured launches are counted once
+    launches_per_step = 7
+    ms_per_step = ms / args.steps
+    value = world * args.tokens * args.steps / (ms / 1000.0)
+
+    # Roofline of the dominant kernel (the tcgen05 expert GEMM: gate_up + down launches).
+    ph, _ = phase_profile(torch, blk, max(10, min(args.steps, 50)))
+    kern_ms = ph["gate_up"] + ph["down"]
+    bytes_step = expert_bytes(args.tokens, U)
+    achieved = bytes_step / (kern_ms / 1000.0) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                "kernel": "expert_gemm_kernel<NF4> (gate_up + down launches of one step)",
+                "algorithmic_bytes_per_step": bytes_step, "distinct_experts": U,
+                "kernel_ms_per_step": round(kern_ms, 4),
+                "phase_ms_per_step": {k: round(v, 4) for k, v in ph.items()},
+                "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
+                "step_frac": round(U * BYTES_PER_EXPERT / (ms_per_step / 1000.0) / 1e9 / hbm_peak, 4)}
+
+    # End to end through the C ABI with host buffers: H2D of x from pinned
+    # memory, the block, D2H of the output, every step.
+    L = rb.lib()
+    nbytes = blk.x.numel() * 2
+    hx = torch.empty_like(blk.x, device="cpu").pin_memory()
+    hx.copy_(blk.x.cpu())
+    hout = torch.empty_like(hx).pin_memory()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def e2e_step():
+        blk.ctx.check(L.riallm_cuda_memcpy_h2d_async(blk.ctx.ptr, blk.x.data_ptr(), hx.data_ptr(), nbytes, st))
+        blk(st)
+        blk.ctx.check(L.riallm_cuda_memcpy_d2h_async(blk.ctx.ptr, hout.data_ptr(), blk.out.data_ptr(), nbytes, st))
+    e2e_ms = timed(torch, e2e_step, args.steps, args.warmup, dist, world)
+    e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
+           "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+           "ms_per_step": round(e2e_ms / args.steps, 4)}
+
+    # Sweep over the other token counts of the configuration (rank-local).
+    sweep = []
+    if not args.no_sweep:
+        for T in SWEEP_T:
+            if T == args.tokens:
+                continue
+            b2 = Block(rb, torch, d, T, device)
+            u2 = b2.distinct_experts()
+            for _ in range(2):
+                b2()
+            steps2 = 5 if T >= 1024 else 20
+            ms2 = timed(torch, b2, steps2, 2, dist, world)
+            ph2, _ = phase_profile(torch, b2, steps2)
+            k2 = ph2["gate_up"] + ph2["down"]
+            entry = {"tokens": T, "tokens_per_s": round(world * T * steps2 / (ms2 / 1000.0), 1),
+                     "ms_per_step": round(ms2 / steps2, 4), "kernel_ms": round(k2, 4),
+                     "distinct_experts": u2}
+            if T >= 1024:
+                tf = expert_flops(T) / (k2 / 1000.0) / 1e12
+                entry.update({"bound": "tensor", "achieved_tflops": round(tf, 1),
+                              "frac_of_burst_peak": round(tf / bf16_peak, 4),
+                              "frac_of_sustained_peak": round(tf / bf16_sust, 4)})
+            else:
+                gbs = expert_bytes(T, u2) / (k2 / 1000.0) / 1e9
+                entry.update({"bound": "hbm", "achieved_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4)})
+            sweep.append(entry)
+            del b2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu_baseline:
+        cpu = cpu_baseline(rb, torch, d, blk)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,0.02) weights (torch cuda generator, seed 2) NF4-quantized; N(0,1) bf16 activations",
+            "config": config_dict(args, world),
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches_note": "7 kernels per step replayed from one CUDA graph (route 3, gather 1, expert GEMMs 2, combine 1)",
+            "captured_launches": per_step_launches,
+            "clocks": clk.summary(), "sweep": sweep,
+        }
+        print(json.dumps(line), flush=True)
+    del g
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def cpu_baseline(rb, torch, d, blk):
+    """The oracle's fp32 CPU port on the same weights, timed on this host's
+    cores on a bounded sample (one full decode batch, repeated)."""
+    import numpy as np
+    from oracle import oracle as O
+    O.build()
+
+    def host_q(q):
+        return O.QTensor(int(q.qtype), q.data.cpu().numpy(), q.scales.cpu().numpy(),
+                         q.zero_points.cpu().numpy(), q.numel, q.block_size)
+    w = O.MoeWeights(host_q(d["mlp.gate.weight"]), host_q(d["mlp.experts.gate_up_proj"]),
+                     host_q(d["mlp.experts.down_proj"]))
+    x = blk.x.view(torch.int16).cpu().numpy().view(np.uint16)
+    threads = os.cpu_count() or 1
+    T = x.shape[0]
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        O.moe_forward(w, x, T, H, I, E, TOP_K, n_threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > 8.0 or reps >= 3:
+            break
+    return {"value": round(T * reps / el, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x full {T}-token decode batch through the fp32 oracle port "
+                      f"(oracle/riallm_oracle.c, OpenMP), same NF4 weights"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--skip-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = dist_setup()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -82,9 +82,12 @@ static inline uint8_t nf4_code(float value) {
 void ro_quantize_nf4(const float* v, uint64_t n, uint8_t* data, float* scales,
                      float* zeros) {
   const uint64_t bs = 64;
-  uint64_t nb = (n + bs - 1) / bs;
-  uint64_t o = 0;
-  for (uint64_t b = 0; b < nb; ++b) {
+  int64_t nb = (int64_t)((n + bs - 1) / bs);
+  /* Blocks are independent; block b's bytes start at 32 b (only the last
+   * block can be shorter than 64 elements). */
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; ++b) {
+    uint64_t o = (uint64_t)b * 32;
     uint64_t start = b * bs;
     uint64_t end = start + bs < n ? start + bs : n;
     uint64_t len = end - start;
@@ -119,9 +122,10 @@ static inline uint8_t rust_as_u8(float t) {
 void ro_quantize_int8(const float* v, uint64_t n, uint8_t* data, float* scales,
                       float* zeros) {
   const uint64_t bs = 128;
-  uint64_t nb = (n + bs - 1) / bs;
-  for (uint64_t b = 0; b < nb; ++b) {
-    uint64_t start = b * bs;
+  int64_t nb = (int64_t)((n + bs - 1) / bs);
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < nb; ++b) {
+    uint64_t start = (uint64_t)b * bs;
     uint64_t end = start + bs < n ? start + bs : n;
     uint64_t len = end - start;
     const float* blk = v + start;

@@ -520,8 +520,17 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
                a.swiglu ? 1 : 0, a.h_out, a.y_out, a.ld_out, a.status};
   auto kern = nf4 ? tc::expert_gemm_kernel<RIALLM_COMPRESSION_FOUR_BIT>
                   : tc::expert_gemm_kernel<RIALLM_COMPRESSION_EIGHT_BIT>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes);
-  if (err != cudaSuccess) return err;
+  // Set the shared-memory opt-in once per device and variant, outside any
+  // stream capture (the first call is never captured: it sizes the arena).
+  static bool attr_done[64][2] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  bool& done = attr_done[dev & 63][nf4 ? 0 : 1];
+  if (!done) {
+    cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    done = true;
+  }
   kern<<<num_sms, tc::kThreads, tc::kSmemBytes, stream>>>(tm_raw, tm_b[0], tm_b[1], tm_b[2], tm_b[3], p);
   return cudaGetLastError();
 }
