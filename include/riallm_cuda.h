@@ -169,6 +169,28 @@ int32_t riallm_cuda_moe_route(riallm_ctx* ctx, const riallm_qtensor* gate,
                               float* topk_w, int32_t* counts, int32_t* offsets,
                               int32_t* perm_pair, void* stream);
 
+/* No counterpart in the reference. The MoE block for callers that cannot
+ * allocate device memory: code whose host owns all device memory, or that
+ * must not call cudaMalloc (it can synchronize the device and has no bounded
+ * latency), and so can neither create a riallm_ctx nor let the library grow
+ * its scratch arena. The caller passes weights, x and out; all scratch comes
+ * from one 24 MiB array compiled into the library, which every GPU that
+ * loads the library holds until the process exits. Nothing is allocated.
+ * Limits: bf16 x/out ([T,H], 16-byte aligned), routed experts only (no
+ * shared expert), the same shape rules as riallm_cuda_moe_forward, and the
+ * call's scratch layout must fit 24 MiB (for hidden 4096 / intermediate
+ * 14336, up to 469 token-expert pairs, T*k); larger calls return
+ * RIALLM_ERR_MEMORY without launching anything. The first call on each
+ * device looks up the array's device address (and sets kernel attributes);
+ * make that first call before any stream capture. Every call reuses the same
+ * array and leaves its contents behind, so calls that overlap on the GPU
+ * (other streams or host threads) race on it: serialize them. Runs on the
+ * current CUDA device and on `stream`. */
+int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, const void* x,
+                                        void* out, int32_t T, int32_t H, int32_t I,
+                                        int32_t E, int32_t k, uint32_t flags,
+                                        void* stream);
+
 /* ---------------------------------------------------------- profiling
  * The reference's Profiler (src/profiler.rs:75-96) times each layer on the
  * host wall clock. Here, when enabled, riallm_cuda_moe_forward records a

@@ -112,6 +112,8 @@ SIGNATURES = {
     "riallm_cuda_profile_enable": (_i32, [_vp, _i32]),
     "riallm_cuda_profile_read": (_i32, [_vp, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_u64)]),
     "riallm_cuda_launch_count": (_u64, [_vp]),
+    "riallm_cuda_moe_forward_noalloc": (_i32, [ctypes.POINTER(CMoeWeights), _vp, _vp, _i32, _i32, _i32,
+                                               _i32, _i32, _u32, _vp]),
 }
 
 PHASES = ("route", "gather", "gate_up", "down", "shared", "combine")

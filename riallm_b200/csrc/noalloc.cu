@@ -1,0 +1,166 @@
+// noalloc.cu -- a MoE block entry point that never allocates device memory.
+//
+// Who needs it: code that runs where cudaMalloc is not available or not
+// allowed -- for example a host that hands this library only pre-planned
+// device memory, a real-time loop that must not call into the allocator
+// (cudaMalloc can synchronize the device and its latency is unbounded), or a
+// plugin host whose own allocator owns all device memory. Such callers can
+// pass their inputs and outputs but cannot let the library grow a scratch
+// arena, and they cannot create a riallm_ctx (creating one allocates).
+//
+// How: the scratch buffers of one block call (router weights, routing
+// results, permutation, permuted activations, SwiGLU product, expert
+// outputs) live in one file-scope __device__ array of kNoAllocScratchBytes.
+// Every GPU that loads the library holds that array until the process exits.
+// The host cannot use the array's name as a device address (on the host it
+// is only a stand-in symbol), so the first call on each device looks the
+// address up with cudaGetSymbolAddress while that device is current and
+// caches it; that first call should therefore happen before any stream
+// capture. All calls share the one array and it keeps the last call's
+// contents: calls that overlap on the GPU (other streams, other host
+// threads) race on it and must be serialized by the caller.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "internal.h"
+
+constexpr uint64_t kNoAllocScratchBytes = 24ull << 20;  // 24 MiB per device
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ __align__(256) int g_noalloc_status;
+
+namespace {
+
+struct DeviceSlot {
+  std::once_flag once;
+  int rc = RIALLM_OK;
+  unsigned char* scratch = nullptr;
+  int* status = nullptr;
+  int num_sms = 0;
+};
+constexpr int kMaxDevices = 64;
+DeviceSlot g_slots[kMaxDevices];
+
+// Per-device set-up, done once with that device current: the device
+// addresses of the scratch array and the status word, and the SM count.
+int device_setup(int dev, DeviceSlot** out) {
+  if (dev < 0 || dev >= kMaxDevices) return RIALLM_ERR_CONFIG;
+  DeviceSlot& s = g_slots[dev];
+  std::call_once(s.once, [&] {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) {
+      s.rc = RIALLM_ERR_CUDA;
+      return;
+    }
+    s.scratch = static_cast<unsigned char*>(p);
+    if (cudaGetSymbolAddress(&p, g_noalloc_status) != cudaSuccess) {
+      s.rc = RIALLM_ERR_CUDA;
+      return;
+    }
+    s.status = static_cast<int*>(p);
+    if (cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      s.rc = RIALLM_ERR_CUDA;
+  });
+  *out = &s;
+  return s.rc;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+bool quantized_ok(const riallm_qtensor& t, uint64_t numel) {
+  if (!t.data || t.numel != numel) return false;
+  if (t.qtype == RIALLM_COMPRESSION_FOUR_BIT) return t.block_size == 64 && t.scales && t.zero_points &&
+                                                     aligned16(t.data) && aligned16(t.scales) &&
+                                                     aligned16(t.zero_points);
+  if (t.qtype == RIALLM_COMPRESSION_EIGHT_BIT) return t.block_size == 128 && t.scales && t.zero_points &&
+                                                      aligned16(t.data) && aligned16(t.scales) &&
+                                                      aligned16(t.zero_points);
+  return false;
+}
+
+}  // namespace
+
+extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, const void* x,
+                                                   void* out, int32_t T, int32_t H, int32_t I,
+                                                   int32_t E, int32_t k, uint32_t flags,
+                                                   void* stream) {
+  if (!w) return RIALLM_ERR_INVALID;
+  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0 || E > 256 || k > 16 || k > E) return RIALLM_ERR_CONFIG;
+  if (H % 256 != 0 || I % 256 != 0) return RIALLM_ERR_CONFIG;
+  if (w->shared_gate_proj.data != nullptr) return RIALLM_ERR_CONFIG;  // routed experts only
+  if (w->gate.data == nullptr || w->gate.numel != (uint64_t)E * H) return RIALLM_ERR_MODEL_LOADING;
+  if (w->gate.qtype != RIALLM_COMPRESSION_NONE && !quantized_ok(w->gate, (uint64_t)E * H))
+    return RIALLM_ERR_QUANTIZATION;
+  if (!quantized_ok(w->gate_up_proj, (uint64_t)E * 2 * I * H) || !quantized_ok(w->down_proj, (uint64_t)E * H * I))
+    return RIALLM_ERR_QUANTIZATION;
+  if (T == 0) return RIALLM_OK;
+  if (!x || !out || !aligned16(x) || !aligned16(out)) return RIALLM_ERR_INVALID;
+
+  // The whole scratch layout of one bf16 block call must fit the array.
+  const rl::MoeLayout L = rl::moe_layout(T, H, I, E, k, RIALLM_DTYPE_BF16, 0);
+  if (L.total > kNoAllocScratchBytes) return RIALLM_ERR_MEMORY;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RIALLM_ERR_CUDA;
+  DeviceSlot* slot = nullptr;
+  if (int rc = device_setup(dev, &slot)) return rc;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* base = reinterpret_cast<char*>(slot->scratch);
+  const int P = T * k;
+  // Only the status word must start at zero; every other buffer is fully
+  // written before it is read within the call.
+  if (cudaMemsetAsync(slot->status, 0, sizeof(int), st) != cudaSuccess) return RIALLM_ERR_CUDA;
+  float* wg = reinterpret_cast<float*>(base + L.wg);
+  int* topk_idx = reinterpret_cast<int*>(base + L.topk_idx);
+  float* topk_w = reinterpret_cast<float*>(base + L.topk_w);
+  int* counts = reinterpret_cast<int*>(base + L.counts);
+  int* offsets = reinterpret_cast<int*>(base + L.offsets);
+  int* perm = reinterpret_cast<int*>(base + L.perm_pair);
+  int* inv = reinterpret_cast<int*>(base + L.inv_pos);
+  if (rl::launch_dequant(w->gate, RIALLM_DEQUANT_REFERENCE, wg, RIALLM_DTYPE_F32, slot->num_sms, st) != cudaSuccess ||
+      rl::launch_router(x, true, wg, T, H, E, k, topk_idx, topk_w, st) != cudaSuccess ||
+      rl::launch_permute(topk_idx, P, E, counts, offsets, perm, inv, st) != cudaSuccess ||
+      rl::launch_gather(x, true, perm, k, P, H, base + L.x_perm, st) != cudaSuccess)
+    return RIALLM_ERR_CUDA;
+
+  rl::TcGemmArgs g{};
+  g.w = w->gate_up_proj;
+  g.K = H;
+  g.rows_per_expert = 2 * I;
+  g.a1_offset = I;
+  g.m_step = 128;
+  g.m_tiles = I / 128;
+  g.b = base + L.x_perm;
+  g.P = P;
+  g.counts = counts;
+  g.offsets = offsets;
+  g.E = E;
+  g.swiglu = true;
+  g.h_out = reinterpret_cast<uint16_t*>(base + L.h_perm);
+  g.ld_out = I;
+  g.status = slot->status;
+  if (rl::launch_tc_gemm(g, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
+  rl::TcGemmArgs d{};
+  d.w = w->down_proj;
+  d.K = I;
+  d.rows_per_expert = H;
+  d.a1_offset = 128;
+  d.m_step = 256;
+  d.m_tiles = H / 256;
+  d.b = base + L.h_perm;
+  d.P = P;
+  d.counts = counts;
+  d.offsets = offsets;
+  d.E = E;
+  d.swiglu = false;
+  d.y_out = reinterpret_cast<float*>(base + L.y_perm);
+  d.ld_out = H;
+  d.status = slot->status;
+  if (rl::launch_tc_gemm(d, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
+  if (rl::launch_combine(reinterpret_cast<float*>(base + L.y_perm), inv, topk_idx, topk_w, T, k, H, nullptr,
+                         nullptr, out, true, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st) != cudaSuccess)
+    return RIALLM_ERR_CUDA;
+  return RIALLM_OK;
+}
