@@ -451,7 +451,8 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
   const int* offsets = (const int*)(base + L.offsets);
   {
     PhaseScope ps(ctx, st, RIALLM_PHASE_GATHER);
-    RL_CUDA(ctx, rl::launch_gather(x, bf16, (const int*)(base + L.perm_pair), k, P, H, base + L.x_perm, st),
+    RL_CUDA(ctx, rl::launch_gather(x, bf16, (const int*)(base + L.perm_pair), k, P, H, base + L.x_perm,
+                                   bf16 && w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st),
             "gather");
     ctx->launches += 1;
   }
@@ -470,9 +471,11 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     g.offsets = offsets;
     g.E = E;
     g.swiglu = true;
+    g.h_pair_perm = w->down_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT;
     g.h_out = (uint16_t*)(base + L.h_perm);
     g.ld_out = I;
     g.status = ctx->d_status;
+    g.max_pairs_per_expert = T;
     {
       PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
       RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
@@ -494,6 +497,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     d.y_out = (float*)(base + L.y_perm);
     d.ld_out = H;
     d.status = ctx->d_status;
+    d.max_pairs_per_expert = T;
     {
       PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
       RL_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");

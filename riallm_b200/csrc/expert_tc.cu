@@ -6,25 +6,47 @@
 // and B holds bf16 activations in expert-sorted pair order.
 //
 // Data path per CTA (persistent, one per SM):
-//   raw-producer warp : TMA (128-byte swizzle, no multicast) of the packed
+//   producer warp     : TMA (128-byte swizzle, no multicast) of the packed
 //                       codes of two 128-row operands, 128 bytes per row per
 //                       stage, into a 3-deep shared-memory ring;
-//   B-producer warp   : TMA of the bf16 token tile (N x 64) per K step;
+//   token warp        : TMA of the bf16 token tile (N x 64) of every K step
+//                       into its own ring, so code prefetch never waits on
+//                       MMA progress;
 //   8 dequant warps   : read codes from shared memory, decode each weight to
 //                       f32 with one LOP3/PRMT and a packed fma.rn.f32x2,
 //                       round to bf16 and write the 128 x 64 A tile straight
 //                       into tensor memory with tcgen05.st (the A operand
 //                       never touches shared memory);
-//   MMA warp          : tcgen05.mma kind::f16, A from TMEM, B from shared
-//                       memory, f32 accumulators D0/D1 in TMEM;
+//   4 MMA warps       : tcgen05.mma kind::f16, A from TMEM, B from shared
+//                       memory, f32 accumulators in TMEM;
 //   4 epilogue warps  : tcgen05.ld of D0/D1 and either h = silu(D0)*D1
 //                       (gate_up, bf16 out) or plain f32 stores (down).
 //
-// Scale/zero parameters are fetched by the dequant threads themselves with
-// cp.async, two stages ahead. NF4 follows the reference decode exactly in
-// its indexing: element 63 of a block uses the next block's scale and zero
-// (src/quantization.rs:55-72), which for the last block of a row is the
-// first block of the next row and, past the tensor's end, scale 1 / zero 0.
+// NF4 scales and zero points ride in the same TMA stage as the codes (a
+// 128-row x 4-block box of each); 8-bit ones are fetched by the dequant
+// threads with cp.async, four stages ahead. NF4 follows the reference decode
+// exactly in its indexing: element 63 of a block uses the next block's scale
+// and zero (src/quantization.rs:55-72) -- for the stage's last block that is
+// the next stage's first, and for a row's last block the next row's first
+// block (loaded once per tile), or past the tensor's end scale 1 / zero 0.
+//
+// MMA issue: one tcgen05.mma occupies its issuing thread for ~160 cycles
+// whatever its N, while MMAs issued from different warps overlap. So four
+// issuer warps each own one accumulator when tiles are at most 64 pairs wide
+// (operand x K half: every sub-stage each issues the 2 K-steps of its half),
+// and two (one per operand) when tiles are 128 wide; the epilogue adds the
+// K halves.
+//
+// Issue cost matters as much: a tcgen05.commit or a barrier wait plus fence
+// costs an issuer about as much as an MMA, so the A ring is organised in
+// stages of 128 K (two 64-K sub-stages per operand) and the token producer
+// arrives on the same "full" barrier as the dequant warps (with its TMA
+// byte count): per stage an issuer does one wait, one fence, its MMAs and
+// one commit.
+//
+// Tensor memory (512 columns): columns [0, 256) hold the accumulators
+// (4 x 64 or 2 x 128 columns), [256, 512) a ring of 2 A stages of 128
+// columns (operand 0 then operand 1; 64 columns = 128 bf16 each).
 //
 // Every wait is bounded (common.cuh); on expiry the CTA raises an abort
 // flag, every role stops, in-flight copies and MMAs are drained with bounded
@@ -37,31 +59,34 @@ namespace rl {
 namespace tc {
 
 constexpr int kRawStages = 3;
-constexpr int kBStages = 4;
-constexpr int kAStages = 4;
-constexpr int kParamSlots = 4;
+constexpr int kBRegionBytes = 64 * 1024;         // token ring: 2 stages x 2 boxes x N x 128 B
+constexpr int kAStages = 2;                      // A ring: 2 stages of 128 K (4 x 64 K sub-stages)
+constexpr int kParamSlots = 6;                   // 8-bit parameter ring (cp.async)
+constexpr int kParamAhead = 4;                   // stages prefetched ahead
 constexpr int kNmax = 128;
-constexpr int kRawOpBytes = 128 * 128;          // one operand: 128 rows x 128 B
-constexpr int kRawStageBytes = 2 * kRawOpBytes;  // 32 KiB
-constexpr int kBStageBytes = kNmax * 128;        // 16 KiB
+constexpr int kRawOpBytes = 128 * 128;           // one operand: 128 rows x 128 B of codes
+constexpr int kRawPrmBytes = 128 * 16;           // one operand's 4 scales (or zeros) per row
+constexpr int kRawStageBytes = 2 * kRawOpBytes + 4 * kRawPrmBytes;  // 40 KiB
+constexpr int kMmaWarps = 4;
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarps = 4;
-constexpr int kWarpRaw = 0, kWarpMma = 1, kWarpB = 2, kWarpDq0 = 3, kWarpEpi0 = 11;
-constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;  // 480
-constexpr int kParamFloats = 8;                          // per thread per slot
+constexpr int kWarpProd = 0, kWarpBProd = 1, kWarpMma0 = 2, kWarpDq0 = kWarpMma0 + kMmaWarps,
+              kWarpEpi0 = kWarpDq0 + kDequantWarps;
+constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;  // 576
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColD0 = 0, kColD1 = 128, kColA = 256;  // A stage s, operand a: kColA + 64 s + 32 a
+constexpr uint32_t kColA = 256;                  // A ring: 2 stages x 128 columns
 constexpr int kMaxE = 256;
 
 constexpr int kSmemRaw = 0;
 constexpr int kSmemB = kSmemRaw + kRawStages * kRawStageBytes;
-constexpr int kSmemPrm = kSmemB + kBStages * kBStageBytes;
-constexpr int kSmemBar = kSmemPrm + kParamSlots * 256 * kParamFloats * 4;
-constexpr int kNumBars = 2 * kRawStages + 2 * kBStages + 2 * kAStages + 3;
-constexpr int kSmemMisc = kSmemBar + 8 * 32;
+constexpr int kSmemPrm = kSmemB + kBRegionBytes;
+constexpr int kSmemBar = kSmemPrm + kParamSlots * 256 * 2 * 4;
+constexpr int kNumBars = 2 * kRawStages + 2 * kAStages + 2 + kMmaWarps;
+constexpr int kSmemMisc = kSmemBar + 8 * 40;
 constexpr int kSmemTab = kSmemMisc + 16;
 constexpr int kSmemBytes = kSmemTab + 4 * (4 * kMaxE + 1) + 1024;  // + alignment slack
-static_assert(kNumBars <= 32, "barrier area");
+static_assert(kNumBars <= 40, "barrier area");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 
 struct Params {
   const float* scales;
@@ -72,10 +97,12 @@ struct Params {
   const int* offsets;
   int E;
   int swiglu;
+  int h_pair_perm;
   uint16_t* h_out;
   float* y_out;
   int ld_out;
   int* status;
+  int d_cols;  // 64 or 128 accumulator columns per operand
 };
 
 struct Tile {
@@ -117,73 +144,93 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 
 __device__ __forceinline__ bool wait_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity))
+  while (!mbar_try_wait_suspend(bar, parity, 2000u))
     if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
   return true;
 }
 
-// Parameter slot of one dequant thread: floats [0,4) scales, [4,8) zeros.
-template <int QT>
-__device__ __forceinline__ void issue_params(float* slot, const Params& p, uint64_t f) {
-  if (QT == RIALLM_COMPRESSION_FOUR_BIT) {
-    if (f + 4 <= p.n_scales) cp_async_16(slot, p.scales + f);
-    else
-      for (int i = 0; i < 4; ++i) slot[i] = (f + i < p.n_scales) ? __ldg(p.scales + f + i) : 1.0f;
-    if (f + 4 <= p.n_zeros) cp_async_16(slot + 4, p.zeros + f);
-    else
-      for (int i = 0; i < 4; ++i) slot[4 + i] = (f + i < p.n_zeros) ? __ldg(p.zeros + f + i) : 0.0f;
-  } else {
-    if (f < p.n_scales) cp_async_4(slot, p.scales + f);
-    else slot[0] = 1.0f;
-    if (f < p.n_zeros) cp_async_4(slot + 4, p.zeros + f);
-    else slot[4] = 0.0f;
+// 8-bit parameter slot of one dequant thread: (scale, zero) of one block.
+__device__ __forceinline__ void issue_params_int8(float* slot, const Params& p, uint64_t f) {
+  if (f < p.n_scales) cp_async_4(slot, p.scales + f);
+  else slot[0] = 1.0f;
+  if (f < p.n_zeros) cp_async_4(slot + 1, p.zeros + f);
+  else slot[1] = 0.0f;
+}
+
+__device__ __forceinline__ uint32_t fma_bf16x2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t sub_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint16_t bf16_bits(float f) {
+  const __nv_bfloat16 b = __float2bfloat16_rn(f);
+  return *reinterpret_cast<const uint16_t*>(&b);
+}
+
+// Block parameters as bf16 pairs: s = hi + lo (hi = bf16(s), lo =
+// bf16(s - hi), together ~16 significant bits) and c = bf16(-z s). Two
+// blocks are split at once: the result's low halves belong to (s0, z0), the
+// high halves to (s1, z1).
+struct Bf16Pair {
+  uint32_t hi, lo, c;
+};
+__device__ __forceinline__ Bf16Pair split_params2(float s0, float z0, float s1, float z1) {
+  Bf16Pair r;
+  r.hi = pack_bf16x2(s0, s1);
+  const float h0 = __uint_as_float(r.hi << 16), h1 = __uint_as_float(r.hi & 0xffff0000u);
+  r.lo = pack_bf16x2(__fsub_rn(s0, h0), __fsub_rn(s1, h1));
+  r.c = pack_bf16x2(__fmul_rn(-z0, s0), __fmul_rn(-z1, s1));
+  return r;
+}
+__device__ __forceinline__ uint32_t lo_lo(uint32_t a, uint32_t b) { return prmt(a, b, 0x5410u); }
+__device__ __forceinline__ uint32_t hi_hi(uint32_t a, uint32_t b) { return prmt(a, b, 0x7632u); }
+__device__ __forceinline__ uint32_t lo_hi(uint32_t a, uint32_t b) { return prmt(a, b, 0x7610u); }
+
+// NF4: decode half (4 words, 32 elements) of a 64-element block into 16
+// bf16x2 registers (element 8i+j is nibble j of word i). Register 4i+j
+// holds elements 8i+j (low half) and 8i+j+4 (high half): one LOP3 of
+// (word >> 4j) against 0x43004300 gives bf16 values 128+q for both, an exact
+// subtraction gives q, and v = q*hi + (q*lo + c) gives (q - z) s to ~2^-17
+// before the final rounding, i.e. the bf16 rounding of the reference's
+// float32 value except at exact ties. Consumers of these A tiles therefore
+// see K permuted inside every group of 8 as [0,4,1,5,2,6,3,7] and the B
+// operand is stored the same way. (hi2, lo2, c2) carry the block's
+// parameters in both halves; (hiL, loL, cL) the block's in the low half and
+// the next block's in the high half, used in the second half's last
+// register, whose high half is element 63.
+template <bool kSecondHalf>
+__device__ __forceinline__ void dequant_nf4_half(const uint4 w4, uint32_t hi2, uint32_t lo2, uint32_t c2,
+                                                 uint32_t hiL, uint32_t loL, uint32_t cL,
+                                                 uint32_t (&out)[16]) {
+  const uint32_t m128 = 0x43004300u;
+  const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t q = sub_bf16x2(and_or(w[i] >> (4 * j), 0x000F000Fu, m128), m128);
+      if (kSecondHalf && i == 3 && j == 3)
+        out[4 * i + j] = fma_bf16x2(q, hiL, fma_bf16x2(q, loL, cL));
+      else
+        out[4 * i + j] = fma_bf16x2(q, hi2, fma_bf16x2(q, lo2, c2));
+    }
   }
 }
 
-// NF4: decode one 64-element block (8 words, element 8i+j = nibble j of
-// word i) into 32 bf16x2 registers. Nibbles are placed in the mantissa of
-// an f32 whose value is 128 + q (bits 16-19) or 2048 + q (bits 12-15), and
-// v = fma(f, s, -(128 + z) s) (resp. 2048) gives (q - z) s; element 63 uses
-// (s2, z2), the next block's parameters.
-__device__ __forceinline__ void dequant_nf4_block(const uint32_t (&w)[8], float s, float z, float s2,
-                                                  float z2, uint32_t (&out)[32]) {
-  const float c16 = -__fmul_rn(__fadd_rn(128.0f, z), s);
-  const float c12 = -__fmul_rn(__fadd_rn(2048.0f, z), s);
-  const float c12n = -__fmul_rn(__fadd_rn(2048.0f, z2), s2);
+// 8-bit: 32 bytes (8 words, 32 elements) -> 16 bf16x2 registers. PRMT
+// places byte j in bits 8-15 of 0x47000000 (value 32768 + q) and
+// v = fma(f, s, -(32768+z) s).
+__device__ __forceinline__ void dequant_int8_half(const uint4 a4, const uint4 b4, float s, float z,
+                                                  uint32_t (&out)[16]) {
+  const float c = -__fmul_rn(__fadd_rn(32768.0f, z), s);
+  const uint32_t w[8] = {a4.x, a4.y, a4.z, a4.w, b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const uint32_t x = w[i];
-    const uint32_t s1 = prmt(x, 0u, 0x4104u);  // byte0 -> byte1, byte1 -> byte2
-    const uint32_t s2b = prmt(x, 0u, 0x4324u); // byte2 -> byte1, byte3 -> byte2
-    const uint32_t s3 = prmt(x, 0u, 0x4034u);  // byte3 -> byte1, byte0 -> byte2
-    const float f0 = __uint_as_float(and_or(s3, 0x000F0000u, 0x43000000u));
-    const float f1 = __uint_as_float(and_or(s1, 0x0000F000u, 0x45000000u));
-    const float f2 = __uint_as_float(and_or(s1, 0x000F0000u, 0x43000000u));
-    const float f3 = __uint_as_float(and_or(x, 0x0000F000u, 0x45000000u));
-    const float f4 = __uint_as_float(and_or(x, 0x000F0000u, 0x43000000u));
-    const float f5 = __uint_as_float(and_or(s2b, 0x0000F000u, 0x45000000u));
-    const float f6 = __uint_as_float(and_or(s2b, 0x000F0000u, 0x43000000u));
-    const float f7 = __uint_as_float(and_or(s3, 0x0000F000u, 0x45000000u));
-    float v0, v1, v2, v3, v4, v5, v6, v7;
-    fma_f32x2(v0, v1, f0, f1, s, s, c16, c12);
-    fma_f32x2(v2, v3, f2, f3, s, s, c16, c12);
-    fma_f32x2(v4, v5, f4, f5, s, s, c16, c12);
-    if (i == 7) fma_f32x2(v6, v7, f6, f7, s, s2, c16, c12n);
-    else fma_f32x2(v6, v7, f6, f7, s, s, c16, c12);
-    out[4 * i + 0] = pack_bf16x2(v0, v1);
-    out[4 * i + 1] = pack_bf16x2(v2, v3);
-    out[4 * i + 2] = pack_bf16x2(v4, v5);
-    out[4 * i + 3] = pack_bf16x2(v6, v7);
-  }
-}
-
-// 8-bit: 64 bytes (16 words) -> 32 bf16x2 registers. PRMT places byte j in
-// bits 8-15 of 0x47000000 (value 32768 + q) and v = fma(f, s, -(32768+z) s).
-__device__ __forceinline__ void dequant_int8_64(const uint32_t (&w)[16], float s, float z,
-                                                uint32_t (&out)[32]) {
-  const float c = -__fmul_rn(__fadd_rn(32768.0f, z), s);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
     const float f0 = __uint_as_float(prmt(w[i], 0x47000000u, 0x7604u));
     const float f1 = __uint_as_float(prmt(w[i], 0x47000000u, 0x7614u));
     const float f2 = __uint_as_float(prmt(w[i], 0x47000000u, 0x7624u));
@@ -199,14 +246,17 @@ __device__ __forceinline__ void dequant_int8_64(const uint32_t (&w)[16], float s
 template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tm_raw,
+                       const __grid_constant__ CUtensorMap tm_scl,
+                       const __grid_constant__ CUtensorMap tm_zer,
                        const __grid_constant__ CUtensorMap tm_b16,
                        const __grid_constant__ CUtensorMap tm_b32,
                        const __grid_constant__ CUtensorMap tm_b64,
                        const __grid_constant__ CUtensorMap tm_b128, const Params p) {
-  constexpr int KR = QT == RIALLM_COMPRESSION_FOUR_BIT ? 256 : 128;  // K per raw stage
-  constexpr int SUB = KR / 64;                                       // A sub-stages per raw stage
-  constexpr int BS = QT == RIALLM_COMPRESSION_FOUR_BIT ? 64 : 128;   // quant block
-  constexpr int PPS = KR / BS;                                       // param blocks per raw stage
+  constexpr bool kNF4 = QT == RIALLM_COMPRESSION_FOUR_BIT;
+  constexpr int KR = kNF4 ? 256 : 128;  // K per raw stage (128 code bytes per row)
+  constexpr int AS_PER_RAW = KR / 128;  // A stages (128 K each) per raw stage
+  constexpr int BS = kNF4 ? 64 : 128;   // quant block
+  constexpr int PPS = KR / BS;          // quant blocks per raw stage
 
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
@@ -216,13 +266,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + kRawStages;
-  uint64_t* b_full = raw_empty + kRawStages;
-  uint64_t* b_empty = b_full + kBStages;
-  uint64_t* a_full = b_empty + kBStages;
-  uint64_t* a_empty = a_full + kAStages;
-  uint64_t* d_full = a_empty + kAStages;
+  uint64_t* full = raw_empty + kRawStages;   // A stage stored + its token tiles landed
+  uint64_t* empty = full + kAStages;         // the stage's MMAs completed
+  uint64_t* d_full = empty + kAStages;
   uint64_t* d_empty = d_full + 1;
-  uint64_t* drain_bar = d_empty + 1;
+  uint64_t* drain_bar = d_empty + 1;         // one per MMA issuer
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + kSmemMisc);
   volatile int* abort_s = reinterpret_cast<volatile int*>(smem + kSmemMisc + 4);
   int* tile_start = reinterpret_cast<int*>(smem + kSmemTab);
@@ -231,23 +279,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* off_s = cnt_s + kMaxE;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Narrow launches (every tile <= 64 pairs): 4 issuers, accumulator of
+  // issuer j = (operand j&1, K half j>>1) at column 64 j. Wide launches:
+  // 2 issuers, accumulator of operand j at column 128 j.
+  const bool narrow = p.d_cols == 64;
+  const int n_iss = narrow ? 4 : 2;
+  const uint32_t b_box = narrow ? 64u * 128u : 128u * 128u;  // one 64-K token box
+  const uint32_t b_stage = 2 * b_box;
 
   if (tid == 0) {
     for (int s = 0; s < kRawStages; ++s) {
       mbar_init(&raw_full[s], 1);
       mbar_init(&raw_empty[s], kDequantWarps);
     }
-    for (int s = 0; s < kBStages; ++s) {
-      mbar_init(&b_full[s], 1);
-      mbar_init(&b_empty[s], 1);
-    }
     for (int s = 0; s < kAStages; ++s) {
-      mbar_init(&a_full[s], kDequantWarps);
-      mbar_init(&a_empty[s], 1);
+      mbar_init(&full[s], kDequantWarps + 1);
+      mbar_init(&empty[s], n_iss);
     }
-    mbar_init(d_full, 1);
+    mbar_init(d_full, n_iss);
     mbar_init(d_empty, kEpiWarps);
-    mbar_init(drain_bar, 1);
+    for (int i = 0; i < kMmaWarps; ++i) mbar_init(&drain_bar[i], 1);
     fence_mbar_init();
     *abort_s = 0;
   }
@@ -266,12 +317,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tile_start[p.E] = acc;
   }
-  if (warp == kWarpMma) {
+  if (warp == kWarpMma0) {
     tmem_alloc(tmem_base_s, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == kWarpRaw && lane == 0) {
+  if (warp == kWarpProd && lane == 0) {
     tma_prefetch_desc(&tm_raw);
+    if (kNF4) {
+      tma_prefetch_desc(&tm_scl);
+      tma_prefetch_desc(&tm_zer);
+    }
+  }
+  if (warp == kWarpBProd && lane == 0) {
     tma_prefetch_desc(&tm_b16);
     tma_prefetch_desc(&tm_b32);
     tma_prefetch_desc(&tm_b64);
@@ -283,13 +340,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_base_s;
   const int total = tile_start[p.E];
   const int n_raw = p.K / KR;
-  const int n_sub = p.K / 64;
+  const int n_as = p.K / 128;  // A stages per tile
 
-  if (warp == kWarpRaw) {
-    // ------------------------------------------------ raw code producer
+  if (warp == kWarpProd) {
+    // ------------------------------------------- producer: codes (+ NF4 params)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      const uint32_t stage_bytes = kNF4 ? (uint32_t)kRawStageBytes : (uint32_t)(2 * kRawOpBytes);
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         Tile ti;
         decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
@@ -299,75 +357,92 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&raw_full[s], kRawStageBytes);
-          tma_load_2d(raw + s * kRawStageBytes, &tm_raw, &raw_full[s], c * 128, ti.row0);
-          tma_load_2d(raw + s * kRawStageBytes + kRawOpBytes, &tm_raw, &raw_full[s], c * 128, ti.row1);
+          uint8_t* st = raw + s * kRawStageBytes;
+          mbar_arrive_expect_tx(&raw_full[s], stage_bytes);
+          tma_load_2d(st, &tm_raw, &raw_full[s], c * 128, ti.row0);
+          tma_load_2d(st + kRawOpBytes, &tm_raw, &raw_full[s], c * 128, ti.row1);
+          if (kNF4) {
+            uint8_t* pp = st + 2 * kRawOpBytes;
+            tma_load_2d(pp, &tm_scl, &raw_full[s], c * PPS, ti.row0);
+            tma_load_2d(pp + kRawPrmBytes, &tm_zer, &raw_full[s], c * PPS, ti.row0);
+            tma_load_2d(pp + 2 * kRawPrmBytes, &tm_scl, &raw_full[s], c * PPS, ti.row1);
+            tma_load_2d(pp + 3 * kRawPrmBytes, &tm_zer, &raw_full[s], c * PPS, ti.row1);
+          }
         }
       }
       // Drain: every issued copy lands before the CTA can exit.
       for (uint32_t j = (it > (uint32_t)kRawStages ? it - kRawStages : 0); j < it; ++j)
         wait_drain(&raw_full[j % kRawStages], (j / kRawStages) & 1);
     }
-  } else if (warp == kWarpB) {
-    // ---------------------------------------------- B (tokens) producer
+  } else if (warp == kWarpBProd) {
+    // ---------------------------------------------- token tile producer
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t ait = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         Tile ti;
         decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
         const CUtensorMap* tm = ti.N == 16 ? &tm_b16 : ti.N == 32 ? &tm_b32 : ti.N == 64 ? &tm_b64 : &tm_b128;
-        const uint32_t bytes = (uint32_t)ti.N * 128u;
-        for (int sub = 0; sub < n_sub; ++sub, ++it) {
-          const int s = it % kBStages;
-          if (!mbar_wait(&b_empty[s], ((it / kBStages) & 1) ^ 1, abort_s, p.status)) {
+        const uint32_t bbytes = (uint32_t)ti.N * 128u;
+        for (int as = 0; as < n_as; ++as, ++ait) {
+          const int s = ait % kAStages;
+          if (!mbar_wait(&empty[s], ((ait / kAStages) & 1) ^ 1, abort_s, p.status)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&b_full[s], bytes);
-          tma_load_2d(bst + s * kBStageBytes, tm, &b_full[s], sub * 64, ti.pos0);
+          uint8_t* bs = bst + s * b_stage;
+          mbar_arrive_expect_tx(&full[s], 2 * bbytes);
+          tma_load_2d(bs, tm, &full[s], as * 128, ti.pos0);
+          tma_load_2d(bs + b_box, tm, &full[s], as * 128 + 64, ti.pos0);
         }
       }
-      for (uint32_t j = (it > (uint32_t)kBStages ? it - kBStages : 0); j < it; ++j)
-        wait_drain(&b_full[j % kBStages], (j / kBStages) & 1);
+      // Drain: the last stages' token copies land before the CTA can exit.
+      for (uint32_t j = (ait > (uint32_t)kAStages ? ait - kAStages : 0); j < ait; ++j)
+        wait_drain(&full[j % kAStages], (j / kAStages) & 1);
     }
-  } else if (warp == kWarpMma) {
-    // -------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      uint32_t ait = 0, bit = 0, tit = 0;
+  } else if (warp < kWarpDq0) {
+    // ------------------------------------------------------- MMA issuers
+    const int j = warp - kWarpMma0;
+    if (lane == 0 && j < n_iss) {
+      const int op = narrow ? (j & 1) : j;        // operand: 0 gate / rows r, 1 up / rows r+128
+      const int kk0 = narrow ? 2 * (j >> 1) : 0;  // first K step of this issuer in a sub-stage
+      const int nkk = narrow ? 2 : 4;
+      const uint32_t d_col = narrow ? 64u * j : 128u * j;
+      uint32_t ait = 0, tit = 0;
       bool ok = true, issued = false;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tit) {
         Tile ti;
         decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
         const uint32_t idesc = idesc_bf16_f32(128, (uint32_t)ti.N);
         if (!mbar_wait(d_empty, (tit & 1) ^ 1, abort_s, p.status)) break;
-        tc_fence_after();
-        for (int sub = 0; sub < n_sub; ++sub, ++ait, ++bit) {
-          const int sa = ait % kAStages, sb = bit % kBStages;
-          if (!mbar_wait(&a_full[sa], (ait / kAStages) & 1, abort_s, p.status) ||
-              !mbar_wait(&b_full[sb], (bit / kBStages) & 1, abort_s, p.status)) {
+        for (int as = 0; as < n_as; ++as, ++ait) {
+          const int s = ait % kAStages;
+          if (!mbar_wait(&full[s], (ait / kAStages) & 1, abort_s, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t bdesc = sdesc_kmajor_sw128(smem_u32(bst + sb * kBStageBytes));
-          const uint32_t a0 = tmem + kColA + sa * 64, a1 = a0 + 32;
+          const uint32_t a_st = tmem + kColA + s * 128 + op * 64;
+          const uint64_t bdesc0 = sdesc_kmajor_sw128(smem_u32(bst + s * b_stage));
+          const uint64_t bdesc1 = sdesc_kmajor_sw128(smem_u32(bst + s * b_stage + b_box));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t acc = (sub | kk) ? 1u : 0u;
-            tc_mma_ts(tmem + kColD0, a0 + kk * 8, bdesc + (uint64_t)(kk * 2), idesc, acc);
-            tc_mma_ts(tmem + kColD1, a1 + kk * 8, bdesc + (uint64_t)(kk * 2), idesc, acc);
+          for (int u = 0; u < 2; ++u) {
+            const uint64_t bdesc = u ? bdesc1 : bdesc0;
+            for (int i = 0; i < nkk; ++i) {
+              const int kk = kk0 + i;
+              tc_mma_ts(tmem + d_col, a_st + u * 32 + kk * 8, bdesc + (uint64_t)(kk * 2), idesc,
+                        (as | u | i) ? 1u : 0u);
+            }
           }
           issued = true;
-          tc_commit(&a_empty[sa]);
-          tc_commit(&b_empty[sb]);
+          tc_commit(&empty[s]);
         }
         if (!ok) break;
         tc_commit(d_full);
       }
       if (issued) {
-        tc_commit(drain_bar);
-        wait_drain(drain_bar, 0);
+        tc_commit(&drain_bar[j]);
+        wait_drain(&drain_bar[j], 0);
       }
     }
   } else if (warp < kWarpEpi0) {
@@ -376,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int a = dw >> 2;                // operand 0 or 1
     const int q = warp & 3;               // TMEM lane quadrant of this warp
     const int r = 32 * q + lane;          // row inside the 128-row operand
-    const int pt = dw * 32 + lane;        // parameter slot owner 0..255
+    const int pt = dw * 32 + lane;        // 8-bit parameter slot owner 0..255
     const int swz = r & 7;
     uint32_t rit = 0, ait = 0;
     bool ok = true;
@@ -386,63 +461,131 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
       const uint64_t rg = (uint64_t)(a ? ti.row1 : ti.row0) + r;
       const uint64_t f0 = rg * blocks_per_row;
-      issue_params<QT>(prm + ((rit + 0) % kParamSlots) * 256 * kParamFloats + pt * kParamFloats, p, f0);
-      cp_async_commit();
-      issue_params<QT>(prm + ((rit + 1) % kParamSlots) * 256 * kParamFloats + pt * kParamFloats, p,
-                       f0 + PPS);
-      cp_async_commit();
+      // NF4: parameters of the element after this row's last one (the next
+      // row's first block, or the reference's 1.0 / 0.0 past the end).
+      float tail_s = 1.0f, tail_z = 0.0f;
+      if (kNF4) {
+        const uint64_t ft = f0 + blocks_per_row;
+        if (ft < p.n_scales) tail_s = __ldg(p.scales + ft);
+        if (ft < p.n_zeros) tail_z = __ldg(p.zeros + ft);
+      } else {
+        for (int c = 0; c < kParamAhead; ++c) {
+          if (c < n_raw)
+            issue_params_int8(prm + ((rit + c) % kParamSlots) * 512 + pt * 2, p, f0 + (uint64_t)c * PPS);
+          cp_async_commit();
+        }
+      }
       for (int c = 0; c < n_raw; ++c, ++rit) {
-        if (c + 2 <= n_raw)
-          issue_params<QT>(prm + ((rit + 2) % kParamSlots) * 256 * kParamFloats + pt * kParamFloats, p,
-                           f0 + (uint64_t)(c + 2) * PPS);
-        cp_async_commit();
-        cp_async_wait<1>();
-        const int s = rit % kRawStages;
-        if (!warp_wait(&raw_full[s], (rit / kRawStages) & 1, abort_s, p.status)) {
+        if (!kNF4) {
+          if (c + kParamAhead < n_raw)
+            issue_params_int8(prm + ((rit + kParamAhead) % kParamSlots) * 512 + pt * 2, p,
+                              f0 + (uint64_t)(c + kParamAhead) * PPS);
+          cp_async_commit();
+          cp_async_wait<kParamAhead>();
+        }
+        const int rs = rit % kRawStages;
+        if (!warp_wait(&raw_full[rs], (rit / kRawStages) & 1, abort_s, p.status)) {
           ok = false;
           break;
         }
-        const float* P0 = prm + (rit % kParamSlots) * 256 * kParamFloats + pt * kParamFloats;
-        const float* P1 = prm + ((rit + 1) % kParamSlots) * 256 * kParamFloats + pt * kParamFloats;
-        const uint8_t* rowp = raw + s * kRawStageBytes + a * kRawOpBytes + r * 128;
-#pragma unroll 1
-        for (int u = 0; u < SUB; ++u, ++ait) {
-          uint32_t regs[32];
-          if (QT == RIALLM_COMPRESSION_FOUR_BIT) {
-            const uint4 c0 = *reinterpret_cast<const uint4*>(rowp + (((2 * u) ^ swz) << 4));
-            const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + (((2 * u + 1) ^ swz) << 4));
-            const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            const float sc = P0[u], ze = P0[4 + u];
-            const float sc2 = u < 3 ? P0[u + 1] : P1[0];
-            const float ze2 = u < 3 ? P0[4 + u + 1] : P1[4];
-            dequant_nf4_block(w, sc, ze, sc2, ze2, regs);
-          } else {
-            uint32_t w[16];
+        const uint8_t* st = raw + rs * kRawStageBytes;
+        const uint8_t* rowp = st + a * kRawOpBytes + r * 128;
+        // NF4: bf16-split parameters of the raw stage's 4 blocks, two per
+        // pair: P01 = (block 0, block 1), P23 = (block 2, block 3).
+        Bf16Pair P01{}, P23{};
+        float next_s = tail_s, next_z = tail_z;
+        if (kNF4) {
+          const float* pp = reinterpret_cast<const float*>(st + 2 * kRawOpBytes + a * 2 * kRawPrmBytes);
+          const float4 sc4 = *reinterpret_cast<const float4*>(pp + r * 4);
+          const float4 ze4 = *reinterpret_cast<const float4*>(pp + kRawPrmBytes / 4 + r * 4);
+          P01 = split_params2(sc4.x, ze4.x, sc4.y, ze4.y);
+          P23 = split_params2(sc4.z, ze4.z, sc4.w, ze4.w);
+        }
+        float sc8 = 0.f, ze8 = 0.f;
+        if (!kNF4) {
+          const float* sl = prm + (rit % kParamSlots) * 512 + pt * 2;
+          sc8 = sl[0];
+          ze8 = sl[1];
+        }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 cj = *reinterpret_cast<const uint4*>(rowp + (((4 * u + j) ^ swz) << 4));
-              w[4 * j + 0] = cj.x;
-              w[4 * j + 1] = cj.y;
-              w[4 * j + 2] = cj.z;
-              w[4 * j + 3] = cj.w;
+        for (int v = 0; v < AS_PER_RAW; ++v, ++ait) {
+          const int s = ait % kAStages;
+          const uint32_t tdst = tmem + ((uint32_t)(32 * q) << 16) + kColA + s * 128 + a * 64;
+          uint32_t regs[16];
+#pragma unroll
+          for (int uu = 0; uu < 2; ++uu) {
+            const int u = 2 * v + uu;  // 64-K sub-stage inside the raw stage
+            if (kNF4) {
+              const uint4 c0 = *reinterpret_cast<const uint4*>(rowp + (((2 * u) ^ swz) << 4));
+              const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + (((2 * u + 1) ^ swz) << 4));
+              if (u == 3 && c + 1 < n_raw) {
+                // The raw stage's last block ends with the next stage's first.
+                const int s1 = (rit + 1) % kRawStages;
+                if (!warp_wait(&raw_full[s1], ((rit + 1) / kRawStages) & 1, abort_s, p.status)) {
+                  ok = false;
+                  break;
+                }
+                const float* pn = reinterpret_cast<const float*>(raw + s1 * kRawStageBytes + 2 * kRawOpBytes +
+                                                                 a * 2 * kRawPrmBytes);
+                next_s = pn[r * 4];
+                next_z = pn[kRawPrmBytes / 4 + r * 4];
+              }
+              // Block u's constants in both halves, and (block u, block u+1)
+              // for the register holding element 63.
+              const Bf16Pair& Pc = (u < 2) ? P01 : P23;
+              uint32_t hi2, lo2, c2, hiL, loL, cL;
+              if ((u & 1) == 0) {
+                hi2 = lo_lo(Pc.hi, Pc.hi); lo2 = lo_lo(Pc.lo, Pc.lo); c2 = lo_lo(Pc.c, Pc.c);
+                hiL = Pc.hi; loL = Pc.lo; cL = Pc.c;
+              } else {
+                hi2 = hi_hi(Pc.hi, Pc.hi); lo2 = hi_hi(Pc.lo, Pc.lo); c2 = hi_hi(Pc.c, Pc.c);
+                if (u == 1) {
+                  // block 1 (low) with block 2, the low half of P23 (high)
+                  hiL = lo_lo(hi2, P23.hi); loL = lo_lo(lo2, P23.lo); cL = lo_lo(c2, P23.c);
+                } else {
+                  const Bf16Pair Pn = split_params2(next_s, next_z, next_s, next_z);
+                  hiL = lo_hi(hi2, Pn.hi); loL = lo_hi(lo2, Pn.lo); cL = lo_hi(c2, Pn.c);
+                }
+              }
+              dequant_nf4_half<false>(c0, hi2, lo2, c2, hiL, loL, cL, regs);
+              if (uu == 0) {
+                // The stage's columns are free once its previous MMAs completed.
+                if (!warp_wait(&empty[s], ((ait / kAStages) & 1) ^ 1, abort_s, p.status)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+              }
+              tmem_st_32x32b_x16(tdst + uu * 32, regs);
+              dequant_nf4_half<true>(c1, hi2, lo2, c2, hiL, loL, cL, regs);
+              tmem_st_32x32b_x16(tdst + uu * 32 + 16, regs);
+            } else {
+              const uint4 ca = *reinterpret_cast<const uint4*>(rowp + (((4 * u) ^ swz) << 4));
+              const uint4 cb = *reinterpret_cast<const uint4*>(rowp + (((4 * u + 1) ^ swz) << 4));
+              dequant_int8_half(ca, cb, sc8, ze8, regs);
+              if (uu == 0) {
+                if (!warp_wait(&empty[s], ((ait / kAStages) & 1) ^ 1, abort_s, p.status)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+              }
+              tmem_st_32x32b_x16(tdst + uu * 32, regs);
+              const uint4 cc = *reinterpret_cast<const uint4*>(rowp + (((4 * u + 2) ^ swz) << 4));
+              const uint4 cd = *reinterpret_cast<const uint4*>(rowp + (((4 * u + 3) ^ swz) << 4));
+              dequant_int8_half(cc, cd, sc8, ze8, regs);
+              tmem_st_32x32b_x16(tdst + uu * 32 + 16, regs);
             }
-            dequant_int8_64(w, P0[0], P0[4], regs);
           }
-          const int sa = ait % kAStages;
-          if (!warp_wait(&a_empty[sa], ((ait / kAStages) & 1) ^ 1, abort_s, p.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          tmem_st_32x32b_x32(tmem + ((uint32_t)(32 * q) << 16) + kColA + sa * 64 + a * 32, regs);
+          if (!ok) break;
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&a_full[sa]);
+          if (lane == 0) mbar_arrive(&full[s]);
         }
         if (!ok) break;
         __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[s]);
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);
       }
     }
     cp_async_wait<0>();
@@ -457,30 +600,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!warp_wait(d_full, tit & 1, abort_s, p.status)) break;
       tc_fence_after();
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-      for (int n0 = 0; n0 < ti.N; n0 += 16) {
-        uint32_t g[16], u[16];
-        tmem_ld_32x32b_x16(lane_base + kColD0 + n0, g);
-        tmem_ld_32x32b_x16(lane_base + kColD1 + n0, u);
-        tmem_wait_ld();
-        if (p.swiglu) {
-          const int col = ti.m_idx * 128 + m;
+      for (int n0 = 0; n0 < ti.N; n0 += 8) {
+        uint32_t g[8], u[8];
+        if (narrow) {
+          // Operand sums over the two K halves: (gate, K half 0) at 0,
+          // (up, 0) at 64, (gate, 1) at 128, (up, 1) at 192.
+          uint32_t g1[8], u1[8];
+          tmem_ld_32x32b_x8(lane_base + n0, g);
+          tmem_ld_32x32b_x8(lane_base + 64 + n0, u);
+          tmem_ld_32x32b_x8(lane_base + 128 + n0, g1);
+          tmem_ld_32x32b_x8(lane_base + 192 + n0, u1);
+          tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (n0 + j < ti.nv) {
-              const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
+          for (int jj = 0; jj < 8; ++jj) {
+            g[jj] = __float_as_uint(__fadd_rn(__uint_as_float(g[jj]), __uint_as_float(g1[jj])));
+            u[jj] = __float_as_uint(__fadd_rn(__uint_as_float(u[jj]), __uint_as_float(u1[jj])));
+          }
+        } else {
+          tmem_ld_32x32b_x8(lane_base + n0, g);
+          tmem_ld_32x32b_x8(lane_base + 128 + n0, u);
+          tmem_wait_ld();
+        }
+        if (p.swiglu) {
+          // When the down projection decodes NF4, h is stored in its K order:
+          // element 8i+r sits at 8i + 2(r%4) + r/4.
+          const int c0 = ti.m_idx * 128 + m;
+          const int col = p.h_pair_perm ? ((c0 & ~7) | ((c0 & 3) << 1) | ((c0 >> 2) & 1)) : c0;
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            if (n0 + jj < ti.nv) {
+              const float gv = __uint_as_float(g[jj]), uv = __uint_as_float(u[jj]);
               const float hv = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
               const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
-              p.h_out[(uint64_t)(ti.pos0 + n0 + j) * p.ld_out + col] = *reinterpret_cast<const uint16_t*>(&hb);
+              p.h_out[(uint64_t)(ti.pos0 + n0 + jj) * p.ld_out + col] = *reinterpret_cast<const uint16_t*>(&hb);
             }
           }
         } else {
           const int col = ti.m_idx * 256 + m;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (n0 + j < ti.nv) {
-              float* yrow = p.y_out + (uint64_t)(ti.pos0 + n0 + j) * p.ld_out;
-              yrow[col] = __uint_as_float(g[j]);
-              yrow[col + 128] = __uint_as_float(u[j]);
+          for (int jj = 0; jj < 8; ++jj) {
+            if (n0 + jj < ti.nv) {
+              float* yrow = p.y_out + (uint64_t)(ti.pos0 + n0 + jj) * p.ld_out;
+              yrow[col] = __uint_as_float(g[jj]);
+              yrow[col + 128] = __uint_as_float(u[jj]);
             }
           }
         }
@@ -492,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
-  if (warp == kWarpMma) {
+  if (warp == kWarpMma0) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -505,10 +667,23 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
   const bool nf4 = a.w.qtype == RIALLM_COMPRESSION_FOUR_BIT;
   const uint64_t row_bytes = nf4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
   const uint64_t total_rows = (uint64_t)a.E * a.rows_per_expert;
-  CUtensorMap tm_raw, tm_b[4];
+  CUtensorMap tm_raw, tm_scl, tm_zer, tm_b[4];
   if (encode_tensor_map_2d(&tm_raw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w.data, row_bytes, total_rows,
                            row_bytes, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
+  if (nf4) {
+    // Scales / zero points viewed as [rows, K/64] float32 (K % 256 == 0 keeps
+    // the 16-byte row stride); a stage reads a 4-block x 128-row box.
+    const uint64_t bpr = (uint64_t)a.K / 64;
+    if (encode_tensor_map_2d(&tm_scl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.w.scales, bpr, total_rows, bpr * 4,
+                             4, 128, CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS ||
+        encode_tensor_map_2d(&tm_zer, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.w.zero_points, bpr, total_rows,
+                             bpr * 4, 4, 128, CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  } else {
+    tm_scl = tm_raw;
+    tm_zer = tm_raw;
+  }
   const uint32_t Ns[4] = {16, 32, 64, 128};
   for (int i = 0; i < 4; ++i)
     if (encode_tensor_map_2d(&tm_b[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b, (uint64_t)a.K,
@@ -517,7 +692,8 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
       return cudaErrorInvalidValue;
   tc::Params p{a.w.scales, a.w.zero_points, a.w.n_scales, a.w.n_zero_points, a.K,
                a.rows_per_expert, a.a1_offset, a.m_step, a.m_tiles, a.counts, a.offsets, a.E,
-               a.swiglu ? 1 : 0, a.h_out, a.y_out, a.ld_out, a.status};
+               a.swiglu ? 1 : 0, a.h_pair_perm ? 1 : 0, a.h_out, a.y_out, a.ld_out, a.status,
+               a.max_pairs_per_expert <= 64 ? 64 : 128};
   auto kern = nf4 ? tc::expert_gemm_kernel<RIALLM_COMPRESSION_FOUR_BIT>
                   : tc::expert_gemm_kernel<RIALLM_COMPRESSION_EIGHT_BIT>;
   // Set the shared-memory opt-in once per device and variant, outside any
@@ -531,7 +707,8 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
     if (err != cudaSuccess) return err;
     done = true;
   }
-  kern<<<num_sms, tc::kThreads, tc::kSmemBytes, stream>>>(tm_raw, tm_b[0], tm_b[1], tm_b[2], tm_b[3], p);
+  kern<<<num_sms, tc::kThreads, tc::kSmemBytes, stream>>>(tm_raw, tm_scl, tm_zer, tm_b[0], tm_b[1], tm_b[2],
+                                                         tm_b[3], p);
   return cudaGetLastError();
 }
 

@@ -9,7 +9,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/riallm_cuda.h"
+#include "riallm_cuda.h"
 
 struct riallm_ctx {
   int device = 0;
@@ -56,9 +56,11 @@ cudaError_t launch_router(const void* x, bool x_bf16, const float* wg, int T, in
 // Counting sort of the T*k (token, choice) pairs by expert.
 cudaError_t launch_permute(const int* topk_idx, int P, int E, int* counts, int* offsets,
                            int* perm_pair, int* inv_pos, cudaStream_t stream);
-// Gathers token rows into expert-sorted pair order.
+// Gathers token rows into expert-sorted pair order. pair_perm (bf16 only)
+// stores each group of 8 columns in the K order of the NF4 tensor-core
+// decode: [0,4,1,5,2,6,3,7].
 cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int k, int P, int H,
-                          void* x_perm, cudaStream_t stream);
+                          void* x_perm, bool pair_perm, cudaStream_t stream);
 // out[t] = sum over t's pairs in expert-ascending order of w * y_perm[pos]
 // (+ shared expert), optional residual add, cast to the activation dtype.
 cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* topk_idx,
@@ -105,10 +107,12 @@ struct TcGemmArgs {
   const int* offsets;
   int E;
   bool swiglu;          // gate_up epilogue (h = silu(D0) * D1) vs down (y = D0 | D1)
+  bool h_pair_perm;     // store h in the NF4 decode's K order (the down weights are NF4)
   uint16_t* h_out;      // [P, ld_out] bf16 when swiglu
   float* y_out;         // [P, ld_out] f32 otherwise
   int ld_out;
   int* status;
+  int max_pairs_per_expert;  // upper bound on any expert's pair count (<= T)
 };
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream);
 

@@ -122,7 +122,8 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   if (rl::launch_dequant(w->gate, RIALLM_DEQUANT_REFERENCE, wg, RIALLM_DTYPE_F32, slot->num_sms, st) != cudaSuccess ||
       rl::launch_router(x, true, wg, T, H, E, k, topk_idx, topk_w, st) != cudaSuccess ||
       rl::launch_permute(topk_idx, P, E, counts, offsets, perm, inv, st) != cudaSuccess ||
-      rl::launch_gather(x, true, perm, k, P, H, base + L.x_perm, st) != cudaSuccess)
+      rl::launch_gather(x, true, perm, k, P, H, base + L.x_perm,
+                        w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st) != cudaSuccess)
     return RIALLM_ERR_CUDA;
 
   rl::TcGemmArgs g{};
@@ -138,9 +139,11 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   g.offsets = offsets;
   g.E = E;
   g.swiglu = true;
+  g.h_pair_perm = w->down_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT;
   g.h_out = reinterpret_cast<uint16_t*>(base + L.h_perm);
   g.ld_out = I;
   g.status = slot->status;
+  g.max_pairs_per_expert = T;
   if (rl::launch_tc_gemm(g, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
   rl::TcGemmArgs d{};
   d.w = w->down_proj;
@@ -158,6 +161,7 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   d.y_out = reinterpret_cast<float*>(base + L.y_perm);
   d.ld_out = H;
   d.status = slot->status;
+  d.max_pairs_per_expert = T;
   if (rl::launch_tc_gemm(d, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
   if (rl::launch_combine(reinterpret_cast<float*>(base + L.y_perm), inv, topk_idx, topk_w, T, k, H, nullptr,
                          nullptr, out, true, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st) != cudaSuccess)

@@ -213,9 +213,10 @@ cudaError_t launch_permute(const int* topk_idx, int P, int E, int* counts, int* 
   return cudaGetLastError();
 }
 
-// One warp per pair row; 16-byte copies.
+// One warp per pair row; 16-byte copies. With pair_perm each 16-byte
+// group of 8 bf16 values is reordered to [0,4,1,5,2,6,3,7].
 __global__ void gather_kernel(const void* __restrict__ x, int x_bf16, const int* __restrict__ perm_pair,
-                              int k, int P, int H, void* __restrict__ x_perm) {
+                              int k, int P, int H, void* __restrict__ x_perm, int pair_perm) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= P) return;
@@ -224,15 +225,28 @@ __global__ void gather_kernel(const void* __restrict__ x, int x_bf16, const int*
   const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(x) + (uint64_t)t * H * esz);
   uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(x_perm) + (uint64_t)row * H * esz);
   const int n16 = H * esz / 16;
-  for (int i = lane; i < n16; i += 32) dst[i] = __ldg(src + i);
+  if (pair_perm) {
+    for (int i = lane; i < n16; i += 32) {
+      const uint4 v = __ldg(src + i);
+      uint4 o;
+      o.x = prmt(v.x, v.z, 0x5410u);
+      o.y = prmt(v.x, v.z, 0x7632u);
+      o.z = prmt(v.y, v.w, 0x5410u);
+      o.w = prmt(v.y, v.w, 0x7632u);
+      dst[i] = o;
+    }
+  } else {
+    for (int i = lane; i < n16; i += 32) dst[i] = __ldg(src + i);
+  }
 }
 
 cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int k, int P, int H,
-                          void* x_perm, cudaStream_t stream) {
+                          void* x_perm, bool pair_perm, cudaStream_t stream) {
   if (P == 0) return cudaSuccess;
   const int warps = 8;
   gather_kernel<<<(P + warps - 1) / warps, warps * 32, 0, stream>>>(x, x_bf16 ? 1 : 0, perm_pair, k,
-                                                                    P, H, x_perm);
+                                                                    P, H, x_perm,
+                                                                    (pair_perm && x_bf16) ? 1 : 0);
   return cudaGetLastError();
 }
 
