@@ -76,6 +76,10 @@ int ensure_arena(riallm_ctx* ctx, uint64_t bytes) {
   const uint64_t sz = align_up(bytes, 2u << 20);
   RL_CUDA(ctx, cudaMalloc(&ctx->arena, sz), "cudaMalloc(arena)");
   ctx->arena_bytes = sz;
+  // The layout's first slot is the router's completion counter, which must
+  // read zero before the first call.
+  RL_CUDA(ctx, cudaMemset(ctx->arena, 0, 1024), "cudaMemset(arena)");
+  RL_CUDA(ctx, cudaDeviceSynchronize(), "cudaDeviceSynchronize");
   return RIALLM_OK;
 }
 
@@ -131,7 +135,7 @@ MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int share
     o = align_up(o + bytes, a);
     return r;
   };
-  L.wg = take((uint64_t)E * H * 4);
+  L.sync = take(4);  // router completion counter, zero between calls
   L.topk_idx = take(P * 4);
   L.topk_w = take(P * 4);
   L.counts = take((uint64_t)E * 4);
@@ -363,17 +367,28 @@ int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I
 
 static int route_into(riallm_ctx* ctx, const riallm_qtensor& gate, const void* x, int T, int H, int E,
                       int k, bool bf16, char* base, const MoeLayout& L, cudaStream_t st) {
-  const int P = T * k;
-  float* wg = (float*)(base + L.wg);
-  RL_CUDA(ctx, rl::launch_dequant(gate, RIALLM_DEQUANT_REFERENCE, wg, RIALLM_DTYPE_F32, ctx->num_sms, st),
-          "router weight dequant");
-  RL_CUDA(ctx, rl::launch_router(x, bf16, wg, T, H, E, k, (int*)(base + L.topk_idx),
-                                 (float*)(base + L.topk_w), st),
-          "router");
-  RL_CUDA(ctx, rl::launch_permute((int*)(base + L.topk_idx), P, E, (int*)(base + L.counts),
-                                  (int*)(base + L.offsets), (int*)(base + L.perm_pair),
-                                  (int*)(base + L.inv_pos), st),
-          "permute");
+  if (gate.qtype == RIALLM_COMPRESSION_NONE && !aligned16(gate.data))
+    return set_err(ctx, RIALLM_ERR_INVALID, "mlp.gate.weight: device buffer must be 16-byte aligned");
+  rl::RouterArgs a{};
+  a.x = x;
+  a.x_bf16 = bf16 ? 1 : 0;
+  a.gdata = gate.data;
+  a.gscales = gate.scales;
+  a.gzeros = gate.zero_points;
+  a.n_scales = gate.n_scales;
+  a.n_zeros = gate.n_zero_points;
+  a.T = T;
+  a.H = H;
+  a.E = E;
+  a.k = k;
+  a.topk_idx = (int*)(base + L.topk_idx);
+  a.topk_w = (float*)(base + L.topk_w);
+  a.counts = (int*)(base + L.counts);
+  a.offsets = (int*)(base + L.offsets);
+  a.perm_pair = (int*)(base + L.perm_pair);
+  a.inv_pos = (int*)(base + L.inv_pos);
+  a.done = (unsigned*)(base + L.sync);
+  RL_CUDA(ctx, rl::launch_router(a, gate.qtype, st), "router");
   return RIALLM_OK;
 }
 

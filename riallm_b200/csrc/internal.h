@@ -38,7 +38,7 @@ namespace rl {
 
 // Offsets of the MoE scratch buffers inside one arena (all 1 KiB aligned).
 struct MoeLayout {
-  uint64_t wg, topk_idx, topk_w, counts, offsets, perm_pair, inv_pos;
+  uint64_t sync, topk_idx, topk_w, counts, offsets, perm_pair, inv_pos;
   uint64_t x_perm, h_perm, y_perm, proj;
   uint64_t sh_g, sh_u, sh_h, sh_y, sh_gate;
   uint64_t total;
@@ -50,12 +50,26 @@ cudaError_t launch_dequant(const riallm_qtensor& t, int mode, void* dst, int dst
 cudaError_t launch_quantize(int qtype, const float* src, uint64_t n, uint8_t* data,
                             float* scales, float* zeros, int num_sms, cudaStream_t stream);
 
-// Router (fixed-order fp32 dot products, own exp, stable top-k).
-cudaError_t launch_router(const void* x, bool x_bf16, const float* wg, int T, int H, int E, int k,
-                          int* topk_idx, float* topk_w, cudaStream_t stream);
-// Counting sort of the T*k (token, choice) pairs by expert.
-cudaError_t launch_permute(const int* topk_idx, int P, int E, int* counts, int* offsets,
-                           int* perm_pair, int* inv_pos, cudaStream_t stream);
+// Router (fixed-order fp32 dot products, own exp, stable top-k) fused with
+// the counting sort of the T*k (token, choice) pairs by expert.
+constexpr int kRouterThreads = 256;
+struct RouterArgs {
+  const void* x;
+  int x_bf16;
+  const void* gdata;  // router weight [E, H]: float32, NF4 or 8-bit codes
+  const float* gscales;
+  const float* gzeros;
+  uint64_t n_scales, n_zeros;
+  int T, H, E, k;
+  int* topk_idx;
+  float* topk_w;
+  int* counts;
+  int* offsets;
+  int* perm_pair;
+  int* inv_pos;
+  unsigned* done;  // zero between calls; the last CTA resets it
+};
+cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stream);
 // Gathers token rows into expert-sorted pair order. pair_perm (bf16 only)
 // stores each group of 8 columns in the K order of the NF4 tensor-core
 // decode: [0,4,1,5,2,6,3,7].

@@ -92,6 +92,7 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   if (w->gate.data == nullptr || w->gate.numel != (uint64_t)E * H) return RIALLM_ERR_MODEL_LOADING;
   if (w->gate.qtype != RIALLM_COMPRESSION_NONE && !quantized_ok(w->gate, (uint64_t)E * H))
     return RIALLM_ERR_QUANTIZATION;
+  if (w->gate.qtype == RIALLM_COMPRESSION_NONE && !aligned16(w->gate.data)) return RIALLM_ERR_INVALID;
   if (!quantized_ok(w->gate_up_proj, (uint64_t)E * 2 * I * H) || !quantized_ok(w->down_proj, (uint64_t)E * H * I))
     return RIALLM_ERR_QUANTIZATION;
   if (T == 0) return RIALLM_OK;
@@ -109,19 +110,37 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* base = reinterpret_cast<char*>(slot->scratch);
   const int P = T * k;
-  // Only the status word must start at zero; every other buffer is fully
-  // written before it is read within the call.
+  // Only the status word must start at zero within the call; the router's
+  // completion counter (the layout's first slot) starts at zero with the
+  // array and the router resets it before it returns. Every other buffer is
+  // fully written before it is read within the call.
   if (cudaMemsetAsync(slot->status, 0, sizeof(int), st) != cudaSuccess) return RIALLM_ERR_CUDA;
-  float* wg = reinterpret_cast<float*>(base + L.wg);
   int* topk_idx = reinterpret_cast<int*>(base + L.topk_idx);
   float* topk_w = reinterpret_cast<float*>(base + L.topk_w);
   int* counts = reinterpret_cast<int*>(base + L.counts);
   int* offsets = reinterpret_cast<int*>(base + L.offsets);
   int* perm = reinterpret_cast<int*>(base + L.perm_pair);
   int* inv = reinterpret_cast<int*>(base + L.inv_pos);
-  if (rl::launch_dequant(w->gate, RIALLM_DEQUANT_REFERENCE, wg, RIALLM_DTYPE_F32, slot->num_sms, st) != cudaSuccess ||
-      rl::launch_router(x, true, wg, T, H, E, k, topk_idx, topk_w, st) != cudaSuccess ||
-      rl::launch_permute(topk_idx, P, E, counts, offsets, perm, inv, st) != cudaSuccess ||
+  rl::RouterArgs ra{};
+  ra.x = x;
+  ra.x_bf16 = 1;
+  ra.gdata = w->gate.data;
+  ra.gscales = w->gate.scales;
+  ra.gzeros = w->gate.zero_points;
+  ra.n_scales = w->gate.n_scales;
+  ra.n_zeros = w->gate.n_zero_points;
+  ra.T = T;
+  ra.H = H;
+  ra.E = E;
+  ra.k = k;
+  ra.topk_idx = topk_idx;
+  ra.topk_w = topk_w;
+  ra.counts = counts;
+  ra.offsets = offsets;
+  ra.perm_pair = perm;
+  ra.inv_pos = inv;
+  ra.done = reinterpret_cast<unsigned*>(base + L.sync);
+  if (rl::launch_router(ra, w->gate.qtype, st) != cudaSuccess ||
       rl::launch_gather(x, true, perm, k, P, H, base + L.x_perm,
                         w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st) != cudaSuccess)
     return RIALLM_ERR_CUDA;

@@ -63,12 +63,19 @@ __global__ void dequant_nf4_kernel(DqParams p, OutT* __restrict__ out) {
       const uint64_t nb = (p.numel + 1) / 2;
       for (int i = 0; i < 16; ++i) bytes[i] = (e0 / 2 + i < nb) ? p.data[e0 / 2 + i] : 0;
     }
+    // Block of element e: (e + 1) / block_size, stepped instead of divided.
+    uint64_t b = (e0 + 1) / p.block_size;
+    uint32_t r = (uint32_t)(e0 + 1 - b * p.block_size);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const uint64_t e = e0 + i;
       if (e >= p.numel) break;
       uint32_t code = (i & 1) ? (bytes[i >> 1] >> 4) & 15u : bytes[i >> 1] & 15u;
-      store_val(out, e, dq_value(p, code, (e + 1) / p.block_size, true));
+      store_val(out, e, dq_value(p, code, b, true));
+      if (++r == p.block_size) {
+        r = 0;
+        ++b;
+      }
     }
   }
 }
@@ -87,11 +94,17 @@ __global__ void dequant_int8_kernel(DqParams p, OutT* __restrict__ out) {
     } else {
       for (int i = 0; i < 16; ++i) bytes[i] = (e0 + i < p.numel) ? p.data[e0 + i] : 0;
     }
+    uint64_t b = e0 / p.block_size;
+    uint32_t r = (uint32_t)(e0 - b * p.block_size);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const uint64_t e = e0 + i;
       if (e >= p.numel) break;
-      store_val(out, e, dq_value(p, bytes[i], e / p.block_size, false));
+      store_val(out, e, dq_value(p, bytes[i], b, false));
+      if (++r == p.block_size) {
+        r = 0;
+        ++b;
+      }
     }
   }
 }

@@ -61,116 +61,65 @@ __device__ __forceinline__ void load_chunk8(const void* x, bool x_bf16, uint64_t
 }
 
 // One warp per token. Shared memory: per warp E logits and E probabilities.
-__global__ void router_kernel(const void* __restrict__ x, int x_bf16, const float* __restrict__ wg,
-                              int T, int H, int E, int k, int* __restrict__ topk_idx,
-                              float* __restrict__ topk_w) {
-  extern __shared__ float sm[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (t >= T) return;
-  float* lg = sm + (size_t)warp * 2 * E;
-  float* pr = lg + E;
-  const int nchunk = H >> 3;
-  const uint64_t xrow = (uint64_t)t * H;
-  for (int e0 = 0; e0 < E; e0 += 8) {
-    const int ne = min(8, E - e0);
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int c = lane; c < nchunk; c += 32) {
-      float xv[8];
-      load_chunk8(x, x_bf16 != 0, xrow + 8ull * c, xv);
+// Eight consecutive elements g0..g0+7 (g0 a multiple of 8) of the router
+// weight as float32, decoded like QuantizedTensor::dequantize
+// (src/quantization.rs:45-95): value = (code - zero) * scale. NF4 element e
+// reads nibble e%2 of byte e/2 and block (e+1)/64, so only element 7 of a
+// chunk can sit in the next block; 8-bit element e reads block e/128. A
+// block past the parameter arrays uses scale 1.0 / zero 0.0.
+template <int QT>
+__device__ __forceinline__ void gate_chunk8(const RouterArgs& a, uint64_t g0, float (&w)[8]) {
+  if (QT == RIALLM_COMPRESSION_NONE) {
+    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.gdata) + g0);
+    const float4 u = __ldg(p), v = __ldg(p + 1);
+    w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+    w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
+  } else if (QT == RIALLM_COMPRESSION_FOUR_BIT) {
+    const uint32_t codes = __ldg(reinterpret_cast<const uint32_t*>(a.gdata) + g0 / 8);
+    const uint64_t b0 = g0 >> 6, b7 = (g0 + 8) >> 6;
+    const float s0 = b0 < a.n_scales ? __ldg(a.gscales + b0) : 1.0f;
+    const float z0 = b0 < a.n_zeros ? __ldg(a.gzeros + b0) : 0.0f;
+    const float s7 = b7 < a.n_scales ? __ldg(a.gscales + b7) : 1.0f;
+    const float z7 = b7 < a.n_zeros ? __ldg(a.gzeros + b7) : 0.0f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (j < ne) {
-          const float4* wp = reinterpret_cast<const float4*>(wg + (uint64_t)(e0 + j) * H + 8ull * c);
-          float4 w0 = __ldg(wp), w1 = __ldg(wp + 1);
-          float a = acc[j];
-          a = __fmaf_rn(xv[0], w0.x, a);
-          a = __fmaf_rn(xv[1], w0.y, a);
-          a = __fmaf_rn(xv[2], w0.z, a);
-          a = __fmaf_rn(xv[3], w0.w, a);
-          a = __fmaf_rn(xv[4], w1.x, a);
-          a = __fmaf_rn(xv[5], w1.y, a);
-          a = __fmaf_rn(xv[6], w1.z, a);
-          a = __fmaf_rn(xv[7], w1.w, a);
-          acc[j] = a;
-        }
-      }
+    for (int i = 0; i < 8; ++i) {
+      const float code = (float)((codes >> (4 * i)) & 15u);
+      w[i] = i == 7 ? __fmul_rn(__fsub_rn(code, z7), s7) : __fmul_rn(__fsub_rn(code, z0), s0);
     }
+  } else {
+    const uint2 codes = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(a.gdata) + g0));
+    const uint64_t b = g0 >> 7;
+    const float s = b < a.n_scales ? __ldg(a.gscales + b) : 1.0f;
+    const float z = b < a.n_zeros ? __ldg(a.gzeros + b) : 0.0f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (j < ne) {
-        float v = acc[j];
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(kFull, v, off));
-        if (lane == 0) lg[e0 + j] = v;
-      }
-    }
-  }
-  __syncwarp();
-  float m = __int_as_float(0xff800000);
-  for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
-  for (int e = lane; e < E; e += 32) pr[e] = own_expf(__fsub_rn(lg[e], m));
-  __syncwarp();
-  if (lane == 0) {
-    float s = 0.0f;
-    for (int e = 0; e < E; ++e) s = __fadd_rn(s, pr[e]);
-    for (int e = 0; e < E; ++e) pr[e] = __fdiv_rn(pr[e], s);
-    // Stable descending selection: strict > keeps the lower index on ties.
-    // lg[] is reused as the "taken" mark.
-    for (int e = 0; e < E; ++e) lg[e] = 0.0f;
-    int sel[16];
-    float ssum = 0.0f;
-    for (int j = 0; j < k; ++j) {
-      int best = -1;
-      for (int e = 0; e < E; ++e) {
-        if (lg[e] != 0.0f) continue;
-        if (best < 0 || pr[e] > pr[best]) best = e;
-      }
-      lg[best] = 1.0f;
-      sel[j] = best;
-    }
-    for (int j = 0; j < k; ++j) ssum = __fadd_rn(ssum, pr[sel[j]]);
-    for (int j = 0; j < k; ++j) {
-      topk_idx[(uint64_t)t * k + j] = sel[j];
-      if (topk_w) topk_w[(uint64_t)t * k + j] = __fdiv_rn(pr[sel[j]], ssum);
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t word = i < 4 ? codes.x : codes.y;
+      const float code = (float)((word >> (8 * (i & 3))) & 255u);
+      w[i] = __fmul_rn(__fsub_rn(code, z), s);
     }
   }
 }
 
-cudaError_t launch_router(const void* x, bool x_bf16, const float* wg, int T, int H, int E, int k,
-                          int* topk_idx, float* topk_w, cudaStream_t stream) {
-  const int warps = 8;
-  const size_t smem = (size_t)warps * 2 * E * sizeof(float);
-  router_kernel<<<(T + warps - 1) / warps, warps * 32, smem, stream>>>(x, x_bf16 ? 1 : 0, wg, T, H,
-                                                                      E, k, topk_idx, topk_w);
-  return cudaGetLastError();
-}
-
-// One CTA of 1024 threads. Pass 1: per-warp expert histograms over
-// contiguous pair segments. Scan: offsets per expert and a base per
-// (warp, expert). Pass 2: each warp walks its segment in order, ranking
-// equal experts inside each 32-pair batch with match_any, so positions are
-// stable (pair order) inside every expert.
-constexpr int kPermMaxE = 256;
-__global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ topk_idx, int P, int E,
-                                                       int* __restrict__ counts, int* __restrict__ offsets,
-                                                       int* __restrict__ perm_pair,
-                                                       int* __restrict__ inv_pos) {
-  __shared__ int hist[32][kPermMaxE + 1];
-  __shared__ int off_s[kPermMaxE + 1];
+// Stable counting sort of the P (token, choice) pairs by expert, run by one
+// CTA of kRouterThreads threads: per-warp histograms over contiguous pair
+// segments, an exclusive scan per expert, then each warp walks its segment
+// in order and ranks equal experts inside every 32-pair batch with
+// match_any, so each expert's pairs keep pair order.
+__device__ void permute_block(const int* topk_idx, int P, int E, int* counts, int* offsets,
+                              int* perm_pair, int* inv_pos, int* hist, int* off_s) {
+  constexpr int W = kRouterThreads / 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < 32 * (kPermMaxE + 1); i += blockDim.x) (&hist[0][0])[i] = 0;
+  const int stride = E + 1;
+  for (int i = tid; i < W * stride; i += kRouterThreads) hist[i] = 0;
   __syncthreads();
-  const int per = (P + 31) / 32;
+  const int per = (P + W - 1) / W;
   const int p0 = min(P, warp * per), p1 = min(P, p0 + per);
-  for (int p = p0 + lane; p < p1; p += 32) atomicAdd(&hist[warp][topk_idx[p]], 1);
+  for (int p = p0 + lane; p < p1; p += 32) atomicAdd(&hist[warp * stride + __ldcg(topk_idx + p)], 1);
   __syncthreads();
-  if (tid < E) {
+  for (int e = tid; e < E; e += kRouterThreads) {
     int c = 0;
-    for (int w = 0; w < 32; ++w) c += hist[w][tid];
-    off_s[tid + 1] = c;
+    for (int w = 0; w < W; ++w) c += hist[w * stride + e];
+    off_s[e + 1] = c;
   }
   __syncthreads();
   if (tid == 0) {
@@ -178,79 +127,161 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int* __restrict__ t
     for (int e = 0; e < E; ++e) off_s[e + 1] += off_s[e];
   }
   __syncthreads();
-  if (tid < E) {
-    int b = off_s[tid];
-    counts[tid] = off_s[tid + 1] - off_s[tid];
-    for (int w = 0; w < 32; ++w) {
-      const int h = hist[w][tid];
-      hist[w][tid] = b;
+  for (int e = tid; e < E; e += kRouterThreads) {
+    int b = off_s[e];
+    counts[e] = off_s[e + 1] - off_s[e];
+    for (int w = 0; w < W; ++w) {
+      const int h = hist[w * stride + e];
+      hist[w * stride + e] = b;
       b += h;
     }
   }
-  if (tid <= E) offsets[tid] = off_s[tid];
+  for (int e = tid; e <= E; e += kRouterThreads) offsets[e] = off_s[e];
   __syncthreads();
   for (int base = p0; base < p1; base += 32) {
     const int p = base + lane;
     const bool valid = p < p1;
     const unsigned act = __ballot_sync(kFull, valid);
     if (valid) {
-      const int e = topk_idx[p];
+      const int e = __ldcg(topk_idx + p);
       const unsigned peers = __match_any_sync(act, e);
       const int rank = __popc(peers & ((1u << lane) - 1u));
-      const int pos = hist[warp][e] + rank;
+      const int pos = hist[warp * stride + e] + rank;
       perm_pair[pos] = p;
       if (inv_pos) inv_pos[p] = pos;
       __syncwarp(act);
-      if (rank == 0) hist[warp][e] += __popc(peers);
+      if (rank == 0) hist[warp * stride + e] += __popc(peers);
     }
     __syncwarp();
   }
 }
 
-cudaError_t launch_permute(const int* topk_idx, int P, int E, int* counts, int* offsets,
-                           int* perm_pair, int* inv_pos, cudaStream_t stream) {
-  permute_kernel<<<1, 1024, 0, stream>>>(topk_idx, P, E, counts, offsets, perm_pair, inv_pos);
+// One CTA per token: warp w computes the logits of experts w, w+8, ...
+// (decoding the router weight on the fly), warp 0 then takes the softmax
+// and the top k. The CTA that finishes last (a counter in device memory,
+// zero between calls and reset by that CTA) sorts all pairs by expert.
+template <int QT>
+__global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs a) {
+  extern __shared__ float sm[];
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x;
+  const int E = a.E, H = a.H, k = a.k;
+  float* lg = sm;
+  float* pr = sm + E;
+  const int nchunk = H >> 3;
+  const uint64_t xrow = (uint64_t)t * H;
+  for (int e = warp; e < E; e += kRouterThreads / 32) {
+    float acc = 0.0f;
+    const uint64_t grow = (uint64_t)e * H;
+#pragma unroll 4
+    for (int c = lane; c < nchunk; c += 32) {
+      float xv[8], wv[8];
+      load_chunk8(a.x, a.x_bf16 != 0, xrow + 8ull * c, xv);
+      gate_chunk8<QT>(a, grow + 8ull * c, wv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc = __fmaf_rn(xv[i], wv[i], acc);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(kFull, acc, off));
+    if (lane == 0) lg[e] = acc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float m = __int_as_float(0xff800000);
+    for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
+    for (int e = lane; e < E; e += 32) pr[e] = own_expf(__fsub_rn(lg[e], m));
+    __syncwarp();
+    if (lane == 0) {
+      float s = 0.0f;
+      for (int e = 0; e < E; ++e) s = __fadd_rn(s, pr[e]);
+      for (int e = 0; e < E; ++e) pr[e] = __fdiv_rn(pr[e], s);
+      // Stable descending selection: strict > keeps the lower index on ties.
+      // lg[] is reused as the "taken" mark.
+      for (int e = 0; e < E; ++e) lg[e] = 0.0f;
+      int sel[16];
+      float ssum = 0.0f;
+      for (int j = 0; j < k; ++j) {
+        int best = -1;
+        for (int e = 0; e < E; ++e) {
+          if (lg[e] != 0.0f) continue;
+          if (best < 0 || pr[e] > pr[best]) best = e;
+        }
+        lg[best] = 1.0f;
+        sel[j] = best;
+      }
+      for (int j = 0; j < k; ++j) ssum = __fadd_rn(ssum, pr[sel[j]]);
+      for (int j = 0; j < k; ++j) {
+        a.topk_idx[(uint64_t)t * k + j] = sel[j];
+        if (a.topk_w) a.topk_w[(uint64_t)t * k + j] = __fdiv_rn(pr[sel[j]], ssum);
+      }
+      __threadfence();
+      is_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    }
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  int* hist = reinterpret_cast<int*>(sm + 2 * E);
+  int* off_s = hist + (kRouterThreads / 32) * (E + 1);
+  permute_block(a.topk_idx, a.T * k, E, a.counts, a.offsets, a.perm_pair, a.inv_pos, hist, off_s);
+  __syncthreads();
+  if (threadIdx.x == 0) *a.done = 0u;
+}
+
+cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stream) {
+  if (a.T <= 0) return cudaSuccess;
+  const size_t smem = (size_t)2 * a.E * sizeof(float) +
+                      (size_t)((kRouterThreads / 32) * (a.E + 1) + a.E + 1) * sizeof(int);
+  if (gate_qtype == RIALLM_COMPRESSION_FOUR_BIT)
+    router_kernel<RIALLM_COMPRESSION_FOUR_BIT><<<a.T, kRouterThreads, smem, stream>>>(a);
+  else if (gate_qtype == RIALLM_COMPRESSION_EIGHT_BIT)
+    router_kernel<RIALLM_COMPRESSION_EIGHT_BIT><<<a.T, kRouterThreads, smem, stream>>>(a);
+  else
+    router_kernel<RIALLM_COMPRESSION_NONE><<<a.T, kRouterThreads, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
 // One warp per pair row; 16-byte copies. With pair_perm each 16-byte
 // group of 8 bf16 values is reordered to [0,4,1,5,2,6,3,7].
-__global__ void gather_kernel(const void* __restrict__ x, int x_bf16, const int* __restrict__ perm_pair,
-                              int k, int P, int H, void* __restrict__ x_perm, int pair_perm) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (row >= P) return;
-  const int t = perm_pair[row] / k;
+// Row blockIdx.x of x_perm, 16-byte chunks blockIdx.y * 256 + threadIdx.x.
+__global__ void __launch_bounds__(256) gather_kernel(const void* __restrict__ x, int x_bf16,
+                                                     const int* __restrict__ perm_pair, int k, int H,
+                                                     void* __restrict__ x_perm, int pair_perm) {
+  const int row = blockIdx.x;
   const int esz = x_bf16 ? 2 : 4;
+  const int n16 = H * esz / 16;
+  const int i = blockIdx.y * blockDim.x + threadIdx.x;
+  if (i >= n16) return;
+  const int t = __ldg(perm_pair + row) / k;
   const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(x) + (uint64_t)t * H * esz);
   uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(x_perm) + (uint64_t)row * H * esz);
-  const int n16 = H * esz / 16;
+  const uint4 v = __ldg(src + i);
   if (pair_perm) {
-    for (int i = lane; i < n16; i += 32) {
-      const uint4 v = __ldg(src + i);
-      uint4 o;
-      o.x = prmt(v.x, v.z, 0x5410u);
-      o.y = prmt(v.x, v.z, 0x7632u);
-      o.z = prmt(v.y, v.w, 0x5410u);
-      o.w = prmt(v.y, v.w, 0x7632u);
-      dst[i] = o;
-    }
+    uint4 o;
+    o.x = prmt(v.x, v.z, 0x5410u);
+    o.y = prmt(v.x, v.z, 0x7632u);
+    o.z = prmt(v.y, v.w, 0x5410u);
+    o.w = prmt(v.y, v.w, 0x7632u);
+    dst[i] = o;
   } else {
-    for (int i = lane; i < n16; i += 32) dst[i] = __ldg(src + i);
+    dst[i] = v;
   }
 }
 
 cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int k, int P, int H,
                           void* x_perm, bool pair_perm, cudaStream_t stream) {
   if (P == 0) return cudaSuccess;
-  const int warps = 8;
-  gather_kernel<<<(P + warps - 1) / warps, warps * 32, 0, stream>>>(x, x_bf16 ? 1 : 0, perm_pair, k,
-                                                                    P, H, x_perm,
-                                                                    (pair_perm && x_bf16) ? 1 : 0);
+  const int n16 = H * (x_bf16 ? 2 : 4) / 16;
+  const dim3 grid(P, (n16 + 255) / 256);
+  gather_kernel<<<grid, 256, 0, stream>>>(x, x_bf16 ? 1 : 0, perm_pair, k, H, x_perm,
+                                          (pair_perm && x_bf16) ? 1 : 0);
   return cudaGetLastError();
 }
 
-// One CTA per token; 4 columns per thread per step. The token's pairs are
+// One CTA per (token, column slice); 4 columns per thread per step. The token's pairs are
 // visited in expert-ascending order (the reference's index_add order,
 // src/model.rs:794-811): acc = acc + y * w, one rounding each, from 0.
 __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __restrict__ inv_pos,
@@ -276,7 +307,7 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
   }
   float gsig = 0.0f;
   if (shared_y) gsig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-shared_gate[t])));
-  for (int h = threadIdx.x * 4; h < H; h += blockDim.x * 4) {
+  for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < H; h += gridDim.y * blockDim.x * 4) {
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     for (int jj = 0; jj < k; ++jj) {
       const int j = ord[jj];
@@ -327,7 +358,8 @@ cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* t
                            cudaStream_t stream) {
   if (T == 0) return cudaSuccess;
   const int threads = H >= 1024 ? 256 : 128;
-  combine_kernel<<<T, threads, 0, stream>>>(y_perm, inv_pos, topk_idx, topk_w, k, H, shared_y,
+  const dim3 grid(T, (H + threads * 4 - 1) / (threads * 4));
+  combine_kernel<<<grid, threads, 0, stream>>>(y_perm, inv_pos, topk_idx, topk_w, k, H, shared_y,
                                             shared_gate, out, out_bf16 ? 1 : 0, add_to_out ? 1 : 0);
   return cudaGetLastError();
 }

@@ -32,18 +32,24 @@ def test_router_golden_bit_exact(rb):
     (333, 2048, 128, 8, 2, True),   # fine-grained 128-expert top-8, 8-bit router
     (4096, 1024, 8, 2, 1, True),
     (50, 512, 16, 4, 1, False),     # float32 activations
+    (200, 2048, 256, 16, 1, True),  # widest supported: 256 experts, top-16
+    (7, 1024, 8, 2, 0, True),       # float32 router weight
 ])
 def test_router_random_bit_exact(rb, oracle_lib, T, H, E, k, qt, bf16):
     O = oracle_lib
     rng = np.random.default_rng(T * 7 + E)
     wg = rng.normal(0, 0.02, (E, H)).astype(np.float32)
-    qwg = O.quantize(wg, qt)
     x = O.synthetic_x(T, H, T + 1, bf16=bf16)
-    _, _, idx_ref, w_ref = O.router(x, O.dequantize(qwg).reshape(E, H), k)
+    if qt == 0:
+        _, _, idx_ref, w_ref = O.router(x, wg, k)
+        dev = torch.from_numpy(wg).cuda()
+    else:
+        qwg = O.quantize(wg, qt)
+        _, _, idx_ref, w_ref = O.router(x, O.dequantize(qwg).reshape(E, H), k)
+        dev = rb.QuantizedTensor(torch.from_numpy(qwg.data).cuda(), (E, H), rb.CompressionType(qt),
+                                 torch.from_numpy(qwg.scales).cuda(), torch.from_numpy(qwg.zero_points).cuda(),
+                                 qwg.block_size)
     counts_ref, offsets_ref, perm_ref = O.bucket(idx_ref, E)
-    dev = rb.QuantizedTensor(torch.from_numpy(qwg.data).cuda(), (E, H), rb.CompressionType(qt),
-                             torch.from_numpy(qwg.scales).cuda(), torch.from_numpy(qwg.zero_points).cuda(),
-                             qwg.block_size)
     xt = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16) if bf16 else torch.from_numpy(x).cuda()
     idx, w, counts, offsets, perm = rb.route(dev, xt, k, E)
     assert np.array_equal(idx.cpu().numpy(), idx_ref)
@@ -58,3 +64,23 @@ def test_router_ties_lower_index(rb):
     wg = torch.zeros(8, 256, device="cuda")
     idx, w, *_ = rb.route(wg, x, 3, 8)
     assert idx.cpu().tolist() == [[0, 1, 2]] * 3
+
+
+def test_router_back_to_back_calls(rb, oracle_lib):
+    """The pair sort runs in whichever CTA finishes last, found through a
+    device counter that each call leaves at zero: consecutive calls with
+    different token counts must each sort all of their own pairs."""
+    O = oracle_lib
+    rng = np.random.default_rng(5)
+    E, H, k = 8, 1024, 2
+    wg = rng.normal(0, 0.02, (E, H)).astype(np.float32)
+    for T in (5, 300, 1, 64, 300):
+        x = O.synthetic_x(T, H, T, bf16=True)
+        _, _, idx_ref, _ = O.router(x, wg, k)
+        counts_ref, offsets_ref, perm_ref = O.bucket(idx_ref, E)
+        xt = torch.from_numpy(x.view(np.int16)).cuda().view(torch.bfloat16)
+        idx, w, counts, offsets, perm = rb.route(torch.from_numpy(wg).cuda(), xt, k, E)
+        assert np.array_equal(idx.cpu().numpy(), idx_ref), T
+        assert np.array_equal(counts.cpu().numpy(), counts_ref), T
+        assert np.array_equal(offsets.cpu().numpy(), offsets_ref), T
+        assert np.array_equal(perm.cpu().numpy(), perm_ref), T
