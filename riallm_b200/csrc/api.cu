@@ -76,9 +76,9 @@ int ensure_arena(riallm_ctx* ctx, uint64_t bytes) {
   const uint64_t sz = align_up(bytes, 2u << 20);
   RL_CUDA(ctx, cudaMalloc(&ctx->arena, sz), "cudaMalloc(arena)");
   ctx->arena_bytes = sz;
-  // The layout's first slot is the router's completion counter, which must
-  // read zero before the first call.
-  RL_CUDA(ctx, cudaMemset(ctx->arena, 0, 1024), "cudaMemset(arena)");
+  // The layout's first kSyncBytes are counters that must read zero before
+  // the first call (each call leaves them at zero).
+  RL_CUDA(ctx, cudaMemset(ctx->arena, 0, rl::kSyncBytes), "cudaMemset(arena)");
   RL_CUDA(ctx, cudaDeviceSynchronize(), "cudaDeviceSynchronize");
   return RIALLM_OK;
 }
@@ -124,7 +124,8 @@ struct PhaseScope {
 
 namespace rl {
 
-MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int shared_I) {
+MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int shared_I, int num_sms,
+                     bool with_sk) {
   MoeLayout L{};
   const uint64_t P = (uint64_t)T * k;
   const uint64_t a = 1024;
@@ -135,7 +136,8 @@ MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int share
     o = align_up(o + bytes, a);
     return r;
   };
-  L.sync = take(4);  // router completion counter, zero between calls
+  L.sync = take(kSyncBytes);
+  L.sk_ws = (with_sk && act_dtype == RIALLM_DTYPE_BF16) ? take(tc_sk_ws_bytes(num_sms, T)) : 0;
   L.topk_idx = take(P * 4);
   L.topk_w = take(P * 4);
   L.counts = take((uint64_t)E * 4);
@@ -287,6 +289,9 @@ int32_t riallm_cuda_stream_synchronize(riallm_ctx* ctx, void* stream) {
   RL_CUDA(ctx, cudaMemcpy(&st, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost), "status read");
   if (st != 0) {
     cudaMemset(ctx->d_status, 0, sizeof(int));
+    // An aborted kernel may leave the arena's call counters non-zero.
+    if (ctx->arena) cudaMemset(ctx->arena, 0, rl::kSyncBytes);
+    cudaDeviceSynchronize();
     return set_err(ctx, st, "a bounded device-side wait expired (kernel aborted)");
   }
   return RIALLM_OK;
@@ -361,7 +366,7 @@ int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I
   if (!ctx) return RIALLM_ERR_INVALID;
   if (int s = check_shapes(ctx, T, H, I, E, k)) return s;
   if (int s = set_device(ctx)) return s;
-  MoeLayout L = rl::moe_layout(T, H, I, E, k, act_dtype, 0);
+  MoeLayout L = rl::moe_layout(T, H, I, E, k, act_dtype, 0, ctx->num_sms);
   return ensure_arena(ctx, L.total);
 }
 
@@ -405,7 +410,7 @@ int32_t riallm_cuda_moe_route(riallm_ctx* ctx, const riallm_qtensor* gate, const
   if (!aligned16(x)) return set_err(ctx, RIALLM_ERR_INVALID, "x must be 16-byte aligned");
   if (int s = set_device(ctx)) return s;
   const bool bf16 = act_dtype == RIALLM_DTYPE_BF16;
-  MoeLayout L = rl::moe_layout(T, H, 256, E, k, act_dtype, 0);
+  MoeLayout L = rl::moe_layout(T, H, 256, E, k, act_dtype, 0, ctx->num_sms, false);
   if (int s = ensure_arena(ctx, L.total)) return s;
   char* base = (char*)ctx->arena;
   cudaStream_t st = (cudaStream_t)stream;
@@ -452,7 +457,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
 
   const bool bf16 = act_dtype == RIALLM_DTYPE_BF16;
   const int P = T * k;
-  MoeLayout L = rl::moe_layout(T, H, I, E, k, act_dtype, Is);
+  MoeLayout L = rl::moe_layout(T, H, I, E, k, act_dtype, Is, ctx->num_sms);
   if (int s = ensure_arena(ctx, L.total)) return s;
   char* base = (char*)ctx->arena;
   cudaStream_t st = (cudaStream_t)stream;
@@ -491,6 +496,8 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     g.ld_out = I;
     g.status = ctx->d_status;
     g.max_pairs_per_expert = T;
+    g.sk_ws = L.sk_ws ? (float*)(base + L.sk_ws) : nullptr;
+    g.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
     {
       PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
       RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
@@ -513,6 +520,8 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     d.ld_out = H;
     d.status = ctx->d_status;
     d.max_pairs_per_expert = T;
+    d.sk_ws = L.sk_ws ? (float*)(base + L.sk_ws) : nullptr;
+    d.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
     {
       PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
       RL_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");

@@ -120,6 +120,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// Prefetch of one 2-D tile of a tensor map into L2 (no shared memory, no
+// barrier). Same coordinate rules as tma_load_2d.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+               : "memory");
+}
+
 // --------------------------------------------------------- cp.async (LDGSTS)
 
 __device__ __forceinline__ void cp_async_16(void* dst, const void* src) {

@@ -8,15 +8,17 @@
 // Data path per CTA (persistent, one per SM):
 //   producer warp     : TMA (128-byte swizzle, no multicast) of the packed
 //                       codes of two 128-row operands, 128 bytes per row per
-//                       stage, into a 3-deep shared-memory ring;
-//   token warp        : TMA of the bf16 token tile (N x 64) of every K step
-//                       into its own ring, so code prefetch never waits on
-//                       MMA progress;
-//   8 dequant warps   : read codes from shared memory, decode each weight to
-//                       f32 with one LOP3/PRMT and a packed fma.rn.f32x2,
-//                       round to bf16 and write the 128 x 64 A tile straight
-//                       into tensor memory with tcgen05.st (the A operand
-//                       never touches shared memory);
+//                       stage, into a 3-deep shared-memory ring, plus L2
+//                       prefetches of the stages four ahead of that ring;
+//   token warp        : TMA of the bf16 token tiles (N x 128 K) of every A
+//                       stage into its own ring slot, so code prefetch
+//                       never waits on MMA progress;
+//   8 dequant warps   : read codes from shared memory, decode each weight
+//                       (NF4: LOP3 + exact bf16x2 subtract + two bf16x2
+//                       FMAs over a split scale; 8-bit: PRMT + fma.rn.f32x2
+//                       + bf16 round) and write the 128 x 128 A tiles
+//                       straight into tensor memory with tcgen05.st (the A
+//                       operand never touches shared memory);
 //   4 MMA warps       : tcgen05.mma kind::f16, A from TMEM, B from shared
 //                       memory, f32 accumulators in TMEM;
 //   4 epilogue warps  : tcgen05.ld of D0/D1 and either h = silu(D0)*D1
@@ -44,9 +46,13 @@
 // byte count): per stage an issuer does one wait, one fence, its MMAs and
 // one commit.
 //
-// Tensor memory (512 columns): columns [0, 256) hold the accumulators
-// (4 x 64 or 2 x 128 columns), [256, 512) a ring of 2 A stages of 128
-// columns (operand 0 then operand 1; 64 columns = 128 bf16 each).
+// Tensor memory (512 columns): the accumulators from column 0 (4 x 32
+// when every tile of the launch holds at most 32 pairs, 4 x 64 for other
+// tiles of at most 64, 2 x 128 for wider ones), then a ring of A stages of
+// 128 columns each (operand 0 then operand 1; 64 columns = 128 bf16): three
+// stages behind 4 x 32 accumulators, two otherwise. The third stage lets
+// the dequant warps run a full stage ahead of MMA completion, which
+// matters most at decode sizes.
 //
 // Every wait is bounded (common.cuh); on expiry the CTA raises an abort
 // flag, every role stops, in-flight copies and MMAs are drained with bounded
@@ -60,7 +66,8 @@ namespace tc {
 
 constexpr int kRawStages = 3;
 constexpr int kBRegionBytes = 64 * 1024;         // token ring: 2 stages x 2 boxes x N x 128 B
-constexpr int kAStages = 2;                      // A ring: 2 stages of 128 K (4 x 64 K sub-stages)
+constexpr int kAStages = 3;                      // A ring: up to 3 stages of 128 K (4 x 64 K sub-stages)
+constexpr int kPrefetchStages = 4;              // raw stages prefetched into L2 ahead of the ring
 constexpr int kParamSlots = 6;                   // 8-bit parameter ring (cp.async)
 constexpr int kParamAhead = 4;                   // stages prefetched ahead
 constexpr int kNmax = 128;
@@ -74,7 +81,6 @@ constexpr int kWarpProd = 0, kWarpBProd = 1, kWarpMma0 = 2, kWarpDq0 = kWarpMma0
               kWarpEpi0 = kWarpDq0 + kDequantWarps;
 constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;  // 576
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColA = 256;                  // A ring: 2 stages x 128 columns
 constexpr int kMaxE = 256;
 
 constexpr int kSmemRaw = 0;
@@ -102,12 +108,61 @@ struct Params {
   float* y_out;
   int ld_out;
   int* status;
-  int d_cols;  // 64 or 128 accumulator columns per operand
+  int d_cols;     // 64 or 128 accumulator columns per operand
+  float* sk_ws;   // split-tile partial sums, one [2][d_cols][128] f32 slot per CTA; null: whole tiles
+  int* sk_flags;  // one counter per CTA, zero between launches
 };
 
 struct Tile {
   int e, m_idx, pos0, nv, N;
   int row0, row1;
+};
+
+// Position in a ring of n stages: stage index and the parity of its
+// current use.
+struct RingPos {
+  int s = 0;
+  uint32_t ph = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++s == n) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
+// The raw stages [r0, r1) of tile t.
+struct Item {
+  Tile ti;
+  int t, r0, r1;
+};
+
+// Work of one CTA. Without a partial-sum workspace: whole tiles b, b + G,
+// b + 2G, ... With one (stream-K): the same whole-tile rounds while at
+// least two full waves of tiles remain, then the remaining tiles' W =
+// tiles x raw-stages units are cut into G equal contiguous shares
+// [W b / G, W (b+1) / G), so every CTA streams the same number of weight
+// bytes whatever the tile count. A tile cut by a share boundary is finished
+// by the CTA holding its first raw stage (its last item), which adds the
+// partial sums the other CTAs published (their first split item). A CTA
+// only ever waits at its last item, after publishing its own partial, so
+// the waits cannot form a cycle.
+struct Sched {
+  uint64_t w, w1;    // stream-K units left: [w, w1)
+  int t, t_end;      // whole tiles left: t, t + G, ... < t_end
+  int sk_tile0;      // first tile of the stream-K region
+  int n_raw;
+  __device__ __forceinline__ void init(bool sk, int total, int n_raw_) {
+    n_raw = n_raw_;
+    t = blockIdx.x;
+    const int G = gridDim.x;
+    const int rounds = total / G >= 2 ? total / G - 1 : 0;
+    sk_tile0 = sk ? rounds * G : total;
+    t_end = sk_tile0;
+    const uint64_t W = (uint64_t)(total - sk_tile0) * n_raw;
+    w = W * blockIdx.x / G;
+    w1 = W * (blockIdx.x + 1) / G;
+  }
 };
 
 __device__ __forceinline__ void decode_tile(int t, const int* tile_start, const int* ntn,
@@ -132,6 +187,46 @@ __device__ __forceinline__ void decode_tile(int t, const int* tile_start, const 
   ti.N = nv <= 16 ? 16 : nv <= 32 ? 32 : nv <= 64 ? 64 : 128;
   ti.row0 = e * p.rows_per_expert + m_idx * p.m_step;
   ti.row1 = ti.row0 + p.a1_offset;
+}
+
+__device__ __forceinline__ bool sched_next(Sched& sc, Item& it, const int* tile_start, const int* ntn,
+                                           const int* cnt_s, const int* off_s, const Params& p) {
+  if (sc.t < sc.t_end) {
+    it.t = sc.t;
+    it.r0 = 0;
+    it.r1 = sc.n_raw;
+    sc.t += gridDim.x;
+  } else {
+    if (sc.w >= sc.w1) return false;
+    const int lt = (int)(sc.w / (uint64_t)sc.n_raw);
+    it.t = sc.sk_tile0 + lt;
+    it.r0 = (int)(sc.w - (uint64_t)lt * sc.n_raw);
+    const uint64_t left = sc.w1 - sc.w;
+    it.r1 = left < (uint64_t)(sc.n_raw - it.r0) ? it.r0 + (int)left : sc.n_raw;
+    sc.w += (uint64_t)(it.r1 - it.r0);
+  }
+  decode_tile(it.t, tile_start, ntn, cnt_s, off_s, p, it.ti);
+  return true;
+}
+
+// Bounded wait until *flag >= target (another CTA's partial sums are
+// published); false on abort or after kWaitLimitNs.
+__device__ __forceinline__ bool wait_flag(const int* flag, int target, volatile int* abort, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v >= target) return true;
+    if ((it & 15u) == 15u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        atomicExch(status, 6 /* RIALLM_ERR_TIMEOUT */);
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
 }
 
 // Wait used by warp-collective roles: every lane polls, and the warp goes on
@@ -273,6 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain_bar = d_empty + 1;         // one per MMA issuer
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + kSmemMisc);
   volatile int* abort_s = reinterpret_cast<volatile int*>(smem + kSmemMisc + 4);
+  int* max_nv_s = reinterpret_cast<int*>(smem + kSmemMisc + 8);
   int* tile_start = reinterpret_cast<int*>(smem + kSmemTab);
   int* ntn = tile_start + kMaxE + 1;
   int* cnt_s = ntn + kMaxE;
@@ -316,6 +412,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc += nt * p.m_tiles;
     }
     tile_start[p.E] = acc;
+    int mx = 0;
+    for (int e = 0; e < p.E; ++e) mx = max(mx, min(cnt_s[e], kNmax));
+    *max_nv_s = mx;
   }
   if (warp == kWarpMma0) {
     tmem_alloc(tmem_base_s, kTmemCols);
@@ -340,7 +439,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_base_s;
   const int total = tile_start[p.E];
   const int n_raw = p.K / KR;
-  const int n_as = p.K / 128;  // A stages per tile
+  const bool sk = p.sk_ws != nullptr;
+  // TMEM: accumulators from column 0, then the A ring. Narrow launches whose
+  // tiles all hold <= 32 pairs use 32-column accumulators (4 x 32) and
+  // three A stages; other narrow launches 4 x 64 and two; wide ones 2 x 128
+  // and two.
+  const bool small_n = narrow && *max_nv_s <= 32;
+  const uint32_t acc_cols = narrow ? (small_n ? 32u : 64u) : 128u;
+  const int n_ring = small_n ? 3 : 2;
+  const uint32_t col_a = narrow ? 4u * acc_cols : 256u;
 
   if (warp == kWarpProd) {
     // ------------------------------------------- producer: codes (+ NF4 params)
@@ -348,10 +455,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       const uint32_t stage_bytes = kNF4 ? (uint32_t)kRawStageBytes : (uint32_t)(2 * kRawOpBytes);
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        Tile ti;
-        decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
-        for (int c = 0; c < n_raw; ++c, ++it) {
+      Sched sc;
+      sc.init(sk, total, n_raw);
+      // L2 prefetch cursor, kPrefetchStages raw stages ahead of the loads:
+      // keeps more HBM reads in flight than the shared-memory ring holds.
+      Sched ps = sc;
+      Item pi;
+      bool pv = sched_next(ps, pi, tile_start, ntn, cnt_s, off_s, p);
+      int pc = pv ? pi.r0 : 0;
+      auto prefetch_next = [&]() {
+        if (!pv) return;
+        tma_prefetch_l2_2d(&tm_raw, pc * 128, pi.ti.row0);
+        tma_prefetch_l2_2d(&tm_raw, pc * 128, pi.ti.row1);
+        if (kNF4) {
+          tma_prefetch_l2_2d(&tm_scl, pc * PPS, pi.ti.row0);
+          tma_prefetch_l2_2d(&tm_zer, pc * PPS, pi.ti.row0);
+          tma_prefetch_l2_2d(&tm_scl, pc * PPS, pi.ti.row1);
+          tma_prefetch_l2_2d(&tm_zer, pc * PPS, pi.ti.row1);
+        }
+        if (++pc == pi.r1) {
+          pv = sched_next(ps, pi, tile_start, ntn, cnt_s, off_s, p);
+          if (pv) pc = pi.r0;
+        }
+      };
+      for (int i = 0; i < kPrefetchStages; ++i) prefetch_next();
+      Item im;
+      while (ok && sched_next(sc, im, tile_start, ntn, cnt_s, off_s, p)) {
+        for (int c = im.r0; c < im.r1; ++c, ++it) {
+          prefetch_next();
           const int s = it % kRawStages;
           if (!mbar_wait(&raw_empty[s], ((it / kRawStages) & 1) ^ 1, abort_s, p.status)) {
             ok = false;
@@ -359,14 +490,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* st = raw + s * kRawStageBytes;
           mbar_arrive_expect_tx(&raw_full[s], stage_bytes);
-          tma_load_2d(st, &tm_raw, &raw_full[s], c * 128, ti.row0);
-          tma_load_2d(st + kRawOpBytes, &tm_raw, &raw_full[s], c * 128, ti.row1);
+          tma_load_2d(st, &tm_raw, &raw_full[s], c * 128, im.ti.row0);
+          tma_load_2d(st + kRawOpBytes, &tm_raw, &raw_full[s], c * 128, im.ti.row1);
           if (kNF4) {
             uint8_t* pp = st + 2 * kRawOpBytes;
-            tma_load_2d(pp, &tm_scl, &raw_full[s], c * PPS, ti.row0);
-            tma_load_2d(pp + kRawPrmBytes, &tm_zer, &raw_full[s], c * PPS, ti.row0);
-            tma_load_2d(pp + 2 * kRawPrmBytes, &tm_scl, &raw_full[s], c * PPS, ti.row1);
-            tma_load_2d(pp + 3 * kRawPrmBytes, &tm_zer, &raw_full[s], c * PPS, ti.row1);
+            tma_load_2d(pp, &tm_scl, &raw_full[s], c * PPS, im.ti.row0);
+            tma_load_2d(pp + kRawPrmBytes, &tm_zer, &raw_full[s], c * PPS, im.ti.row0);
+            tma_load_2d(pp + 2 * kRawPrmBytes, &tm_scl, &raw_full[s], c * PPS, im.ti.row1);
+            tma_load_2d(pp + 3 * kRawPrmBytes, &tm_zer, &raw_full[s], c * PPS, im.ti.row1);
           }
         }
       }
@@ -378,15 +509,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------- token tile producer
     if (lane == 0) {
       uint32_t ait = 0;
+      RingPos rp;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        Tile ti;
-        decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
+      Sched sc;
+      sc.init(sk, total, n_raw);
+      Item im;
+      while (ok && sched_next(sc, im, tile_start, ntn, cnt_s, off_s, p)) {
+        const Tile& ti = im.ti;
         const CUtensorMap* tm = ti.N == 16 ? &tm_b16 : ti.N == 32 ? &tm_b32 : ti.N == 64 ? &tm_b64 : &tm_b128;
         const uint32_t bbytes = (uint32_t)ti.N * 128u;
-        for (int as = 0; as < n_as; ++as, ++ait) {
-          const int s = ait % kAStages;
-          if (!mbar_wait(&empty[s], ((ait / kAStages) & 1) ^ 1, abort_s, p.status)) {
+        for (int as = im.r0 * AS_PER_RAW; as < im.r1 * AS_PER_RAW; ++as, ++ait, rp.next(n_ring)) {
+          const int s = rp.s;
+          if (!mbar_wait(&empty[s], rp.ph ^ 1, abort_s, p.status)) {
             ok = false;
             break;
           }
@@ -397,8 +531,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Drain: the last stages' token copies land before the CTA can exit.
-      for (uint32_t j = (ait > (uint32_t)kAStages ? ait - kAStages : 0); j < ait; ++j)
-        wait_drain(&full[j % kAStages], (j / kAStages) & 1);
+      for (uint32_t j = (ait > (uint32_t)n_ring ? ait - n_ring : 0); j < ait; ++j)
+        wait_drain(&full[j % n_ring], (j / n_ring) & 1);
     }
   } else if (warp < kWarpDq0) {
     // ------------------------------------------------------- MMA issuers
@@ -407,22 +541,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int op = narrow ? (j & 1) : j;        // operand: 0 gate / rows r, 1 up / rows r+128
       const int kk0 = narrow ? 2 * (j >> 1) : 0;  // first K step of this issuer in a sub-stage
       const int nkk = narrow ? 2 : 4;
-      const uint32_t d_col = narrow ? 64u * j : 128u * j;
-      uint32_t ait = 0, tit = 0;
+      const uint32_t d_col = acc_cols * j;
+      RingPos rp;
+      uint32_t tit = 0;
       bool ok = true, issued = false;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tit) {
-        Tile ti;
-        decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
-        const uint32_t idesc = idesc_bf16_f32(128, (uint32_t)ti.N);
+      Sched sc;
+      sc.init(sk, total, n_raw);
+      Item im;
+      while (ok && sched_next(sc, im, tile_start, ntn, cnt_s, off_s, p)) {
+        const uint32_t idesc = idesc_bf16_f32(128, (uint32_t)im.ti.N);
         if (!mbar_wait(d_empty, (tit & 1) ^ 1, abort_s, p.status)) break;
-        for (int as = 0; as < n_as; ++as, ++ait) {
-          const int s = ait % kAStages;
-          if (!mbar_wait(&full[s], (ait / kAStages) & 1, abort_s, p.status)) {
+        const int as0 = im.r0 * AS_PER_RAW;
+        for (int as = as0; as < im.r1 * AS_PER_RAW; ++as, rp.next(n_ring)) {
+          const int s = rp.s;
+          if (!mbar_wait(&full[s], rp.ph, abort_s, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_st = tmem + kColA + s * 128 + op * 64;
+          const uint32_t a_st = tmem + col_a + s * 128 + op * 64;
           const uint64_t bdesc0 = sdesc_kmajor_sw128(smem_u32(bst + s * b_stage));
           const uint64_t bdesc1 = sdesc_kmajor_sw128(smem_u32(bst + s * b_stage + b_box));
 #pragma unroll
@@ -431,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < nkk; ++i) {
               const int kk = kk0 + i;
               tc_mma_ts(tmem + d_col, a_st + u * 32 + kk * 8, bdesc + (uint64_t)(kk * 2), idesc,
-                        (as | u | i) ? 1u : 0u);
+                        ((as - as0) | u | i) ? 1u : 0u);
             }
           }
           issued = true;
@@ -439,6 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         tc_commit(d_full);
+        ++tit;
       }
       if (issued) {
         tc_commit(&drain_bar[j]);
@@ -453,31 +591,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = 32 * q + lane;          // row inside the 128-row operand
     const int pt = dw * 32 + lane;        // 8-bit parameter slot owner 0..255
     const int swz = r & 7;
-    uint32_t rit = 0, ait = 0;
+    uint32_t rit = 0;
+    RingPos rp;
     bool ok = true;
     const uint64_t blocks_per_row = (uint64_t)(p.K / BS);
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      Tile ti;
-      decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
+    Sched sc;
+    sc.init(sk, total, n_raw);
+    Item im;
+    while (ok && sched_next(sc, im, tile_start, ntn, cnt_s, off_s, p)) {
+      const Tile& ti = im.ti;
       const uint64_t rg = (uint64_t)(a ? ti.row1 : ti.row0) + r;
       const uint64_t f0 = rg * blocks_per_row;
-      // NF4: parameters of the element after this row's last one (the next
-      // row's first block, or the reference's 1.0 / 0.0 past the end).
-      float tail_s = 1.0f, tail_z = 0.0f;
-      if (kNF4) {
-        const uint64_t ft = f0 + blocks_per_row;
-        if (ft < p.n_scales) tail_s = __ldg(p.scales + ft);
-        if (ft < p.n_zeros) tail_z = __ldg(p.zeros + ft);
-      } else {
+      if (!kNF4) {
         for (int c = 0; c < kParamAhead; ++c) {
-          if (c < n_raw)
-            issue_params_int8(prm + ((rit + c) % kParamSlots) * 512 + pt * 2, p, f0 + (uint64_t)c * PPS);
+          if (im.r0 + c < im.r1)
+            issue_params_int8(prm + ((rit + c) % kParamSlots) * 512 + pt * 2, p, f0 + (uint64_t)(im.r0 + c) * PPS);
           cp_async_commit();
         }
       }
-      for (int c = 0; c < n_raw; ++c, ++rit) {
-        if (!kNF4) {
-          if (c + kParamAhead < n_raw)
+      for (int c = im.r0; c < im.r1; ++c, ++rit) {
+        // NF4: element 63 of the stage's last block takes the parameters of
+        // the block after it -- the next stage's first, the next row's first
+        // for the row's last stage, or 1.0 / 0.0 past the tensor's end.
+        float next_s = 1.0f, next_z = 0.0f;
+        if (kNF4) {
+          const uint64_t nb = f0 + (uint64_t)(c + 1) * PPS;
+          if (nb < p.n_scales) next_s = __ldg(p.scales + nb);
+          if (nb < p.n_zeros) next_z = __ldg(p.zeros + nb);
+        } else {
+          if (c + kParamAhead < im.r1)
             issue_params_int8(prm + ((rit + kParamAhead) % kParamSlots) * 512 + pt * 2, p,
                               f0 + (uint64_t)(c + kParamAhead) * PPS);
           cp_async_commit();
@@ -493,7 +635,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // NF4: bf16-split parameters of the raw stage's 4 blocks, two per
         // pair: P01 = (block 0, block 1), P23 = (block 2, block 3).
         Bf16Pair P01{}, P23{};
-        float next_s = tail_s, next_z = tail_z;
         if (kNF4) {
           const float* pp = reinterpret_cast<const float*>(st + 2 * kRawOpBytes + a * 2 * kRawPrmBytes);
           const float4 sc4 = *reinterpret_cast<const float4*>(pp + r * 4);
@@ -508,28 +649,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           ze8 = sl[1];
         }
 #pragma unroll
-        for (int v = 0; v < AS_PER_RAW; ++v, ++ait) {
-          const int s = ait % kAStages;
-          const uint32_t tdst = tmem + ((uint32_t)(32 * q) << 16) + kColA + s * 128 + a * 64;
-          uint32_t regs[16];
+        for (int v = 0; v < AS_PER_RAW; ++v, rp.next(n_ring)) {
+          const int s = rp.s;
+          const uint32_t tdst = tmem + ((uint32_t)(32 * q) << 16) + col_a + s * 128 + a * 64;
+          uint32_t regs[16], r32[32];
 #pragma unroll
           for (int uu = 0; uu < 2; ++uu) {
             const int u = 2 * v + uu;  // 64-K sub-stage inside the raw stage
             if (kNF4) {
               const uint4 c0 = *reinterpret_cast<const uint4*>(rowp + (((2 * u) ^ swz) << 4));
               const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + (((2 * u + 1) ^ swz) << 4));
-              if (u == 3 && c + 1 < n_raw) {
-                // The raw stage's last block ends with the next stage's first.
-                const int s1 = (rit + 1) % kRawStages;
-                if (!warp_wait(&raw_full[s1], ((rit + 1) / kRawStages) & 1, abort_s, p.status)) {
-                  ok = false;
-                  break;
-                }
-                const float* pn = reinterpret_cast<const float*>(raw + s1 * kRawStageBytes + 2 * kRawOpBytes +
-                                                                 a * 2 * kRawPrmBytes);
-                next_s = pn[r * 4];
-                next_z = pn[kRawPrmBytes / 4 + r * 4];
-              }
               // Block u's constants in both halves, and (block u, block u+1)
               // for the register holding element 63.
               const Bf16Pair& Pc = (u < 2) ? P01 : P23;
@@ -547,24 +676,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                   hiL = lo_hi(hi2, Pn.hi); loL = lo_hi(lo2, Pn.lo); cL = lo_hi(c2, Pn.c);
                 }
               }
-              dequant_nf4_half<false>(c0, hi2, lo2, c2, hiL, loL, cL, regs);
+              // Both halves of the sub-stage, then one 32-column store.
+              dequant_nf4_half<false>(c0, hi2, lo2, c2, hiL, loL, cL, *reinterpret_cast<uint32_t(*)[16]>(r32));
+              dequant_nf4_half<true>(c1, hi2, lo2, c2, hiL, loL, cL, *reinterpret_cast<uint32_t(*)[16]>(r32 + 16));
               if (uu == 0) {
                 // The stage's columns are free once its previous MMAs completed.
-                if (!warp_wait(&empty[s], ((ait / kAStages) & 1) ^ 1, abort_s, p.status)) {
+                if (!warp_wait(&empty[s], rp.ph ^ 1, abort_s, p.status)) {
                   ok = false;
                   break;
                 }
                 tc_fence_after();
               }
-              tmem_st_32x32b_x16(tdst + uu * 32, regs);
-              dequant_nf4_half<true>(c1, hi2, lo2, c2, hiL, loL, cL, regs);
-              tmem_st_32x32b_x16(tdst + uu * 32 + 16, regs);
+              tmem_st_32x32b_x32(tdst + uu * 32, r32);
             } else {
               const uint4 ca = *reinterpret_cast<const uint4*>(rowp + (((4 * u) ^ swz) << 4));
               const uint4 cb = *reinterpret_cast<const uint4*>(rowp + (((4 * u + 1) ^ swz) << 4));
               dequant_int8_half(ca, cb, sc8, ze8, regs);
               if (uu == 0) {
-                if (!warp_wait(&empty[s], ((ait / kAStages) & 1) ^ 1, abort_s, p.status)) {
+                if (!warp_wait(&empty[s], rp.ph ^ 1, abort_s, p.status)) {
                   ok = false;
                   break;
                 }
@@ -587,29 +716,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&raw_empty[rs]);
       }
+      if (!kNF4) cp_async_wait<0>();
     }
     cp_async_wait<0>();
   } else {
     // ------------------------------------------------------- epilogue
     const int q = warp & 3;
     const int m = 32 * q + lane;
+    const uint64_t G = gridDim.x;
+    const uint64_t slot_floats = 2ull * (uint64_t)p.d_cols * 128ull;
     uint32_t tit = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++tit) {
-      Tile ti;
-      decode_tile(t, tile_start, ntn, cnt_s, off_s, p, ti);
+    Sched sc;
+    sc.init(sk, total, n_raw);
+    const uint64_t W = (uint64_t)(total - sc.sk_tile0) * n_raw;  // stream-K units
+    Item im;
+    while (sched_next(sc, im, tile_start, ntn, cnt_s, off_s, p)) {
+      const Tile& ti = im.ti;
+      // part: a later K range of a tile another CTA finishes; owner: this
+      // CTA holds the tile's first raw stage but not its last.
+      const bool part = sk && im.r0 > 0;
+      const bool owner = sk && im.r0 == 0 && im.r1 < n_raw;
+      const uint64_t tile_end = (uint64_t)(im.t - sc.sk_tile0 + 1) * n_raw;  // in stream-K units
       if (!warp_wait(d_full, tit & 1, abort_s, p.status)) break;
       tc_fence_after();
+      bool ok = true;
+      if (owner) {
+        // Every CTA whose share starts inside this tile published a partial.
+        for (uint64_t b2 = blockIdx.x + 1; b2 < G && ok; ++b2) {
+          const uint64_t s0 = W * b2 / G;
+          if (s0 >= tile_end) break;
+          if (W * (b2 + 1) / G == s0) continue;
+          int got = 1;
+          if (lane == 0) got = wait_flag(p.sk_flags + b2, kEpiWarps, abort_s, p.status) ? 1 : 0;
+          ok = __shfl_sync(0xffffffffu, got, 0) != 0;
+        }
+        if (!ok) break;
+      }
+      float* my_slot = part ? p.sk_ws + (uint64_t)blockIdx.x * slot_floats : nullptr;
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
       for (int n0 = 0; n0 < ti.N; n0 += 8) {
         uint32_t g[8], u[8];
         if (narrow) {
           // Operand sums over the two K halves: (gate, K half 0) at 0,
-          // (up, 0) at 64, (gate, 1) at 128, (up, 1) at 192.
+          // (up, 0) at acc_cols, (gate, 1) at 2 acc_cols, (up, 1) at 3.
           uint32_t g1[8], u1[8];
           tmem_ld_32x32b_x8(lane_base + n0, g);
-          tmem_ld_32x32b_x8(lane_base + 64 + n0, u);
-          tmem_ld_32x32b_x8(lane_base + 128 + n0, g1);
-          tmem_ld_32x32b_x8(lane_base + 192 + n0, u1);
+          tmem_ld_32x32b_x8(lane_base + acc_cols + n0, u);
+          tmem_ld_32x32b_x8(lane_base + 2 * acc_cols + n0, g1);
+          tmem_ld_32x32b_x8(lane_base + 3 * acc_cols + n0, u1);
           tmem_wait_ld();
 #pragma unroll
           for (int jj = 0; jj < 8; ++jj) {
@@ -620,6 +774,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x8(lane_base + n0, g);
           tmem_ld_32x32b_x8(lane_base + 128 + n0, u);
           tmem_wait_ld();
+        }
+        if (part) {
+          // [operand][column][row] so a warp's 32 rows store 128 bytes.
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) {
+            my_slot[(uint64_t)(n0 + jj) * 128 + m] = __uint_as_float(g[jj]);
+            my_slot[(uint64_t)(p.d_cols + n0 + jj) * 128 + m] = __uint_as_float(u[jj]);
+          }
+          continue;
+        }
+        if (owner) {
+          // Add the later K ranges in CTA (= K) order: deterministic.
+          for (uint64_t b2 = blockIdx.x + 1; b2 < G; ++b2) {
+            const uint64_t s0 = W * b2 / G;
+            if (s0 >= tile_end) break;
+            if (W * (b2 + 1) / G == s0) continue;
+            const float* ws = p.sk_ws + b2 * slot_floats;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+              g[jj] = __float_as_uint(__fadd_rn(__uint_as_float(g[jj]), __ldcg(ws + (uint64_t)(n0 + jj) * 128 + m)));
+              u[jj] = __float_as_uint(
+                  __fadd_rn(__uint_as_float(u[jj]), __ldcg(ws + (uint64_t)(p.d_cols + n0 + jj) * 128 + m)));
+            }
+          }
         }
         if (p.swiglu) {
           // When the down projection decodes NF4, h is stored in its K order:
@@ -650,6 +828,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(d_empty);
+      ++tit;
+      if (part) {
+        // Publish this warp's rows: the owner waits for all four warps.
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.sk_flags + blockIdx.x, 1);
+      }
+      if (owner) {
+        // Release the partials read: the last of the four reader warps
+        // returns each counter to zero for the next launch.
+        for (uint64_t b2 = blockIdx.x + 1; b2 < G; ++b2) {
+          const uint64_t s0 = W * b2 / G;
+          if (s0 >= tile_end) break;
+          if (W * (b2 + 1) / G == s0) continue;
+          if (lane == 0 && atomicAdd(p.sk_flags + b2, 1) == 2 * kEpiWarps - 1) atomicExch(p.sk_flags + b2, 0);
+        }
+      }
     }
   }
 
@@ -693,7 +888,7 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
   tc::Params p{a.w.scales, a.w.zero_points, a.w.n_scales, a.w.n_zero_points, a.K,
                a.rows_per_expert, a.a1_offset, a.m_step, a.m_tiles, a.counts, a.offsets, a.E,
                a.swiglu ? 1 : 0, a.h_pair_perm ? 1 : 0, a.h_out, a.y_out, a.ld_out, a.status,
-               a.max_pairs_per_expert <= 64 ? 64 : 128};
+               a.max_pairs_per_expert <= 64 ? 64 : 128, a.sk_ws, a.sk_flags};
   auto kern = nf4 ? tc::expert_gemm_kernel<RIALLM_COMPRESSION_FOUR_BIT>
                   : tc::expert_gemm_kernel<RIALLM_COMPRESSION_EIGHT_BIT>;
   // Set the shared-memory opt-in once per device and variant, outside any

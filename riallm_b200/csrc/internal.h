@@ -37,13 +37,20 @@ struct riallm_ctx {
 namespace rl {
 
 // Offsets of the MoE scratch buffers inside one arena (all 1 KiB aligned).
+// The first kSyncBytes of a layout hold counters that must read zero
+// between calls: the router's completion counter at offset 0 and the
+// expert GEMM's split-tile counters (one per SM) from kSkFlagsOffset.
+constexpr uint64_t kSyncBytes = 4096;
+constexpr uint64_t kSkFlagsOffset = 256;
 struct MoeLayout {
-  uint64_t sync, topk_idx, topk_w, counts, offsets, perm_pair, inv_pos;
+  uint64_t sync, sk_ws, topk_idx, topk_w, counts, offsets, perm_pair, inv_pos;
   uint64_t x_perm, h_perm, y_perm, proj;
   uint64_t sh_g, sh_u, sh_h, sh_y, sh_gate;
   uint64_t total;
 };
-MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int shared_I);
+// with_sk: reserve the expert GEMM's split-tile workspace (bf16 only).
+MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int shared_I, int num_sms,
+                     bool with_sk = true);
 
 cudaError_t launch_dequant(const riallm_qtensor& t, int mode, void* dst, int dst_dtype,
                            int num_sms, cudaStream_t stream);
@@ -127,7 +134,14 @@ struct TcGemmArgs {
   int ld_out;
   int* status;
   int max_pairs_per_expert;  // upper bound on any expert's pair count (<= T)
+  float* sk_ws;              // split-tile partial sums, tc_sk_ws_bytes(); null: whole tiles per CTA
+  int* sk_flags;             // num_sms counters, zero between launches
 };
+// Bytes of the split-tile workspace of launch_tc_gemm: one slot of
+// 2 operands x 128 rows x (64 or 128) f32 columns per CTA (= per SM).
+inline uint64_t tc_sk_ws_bytes(int num_sms, int max_pairs_per_expert) {
+  return (uint64_t)num_sms * 2u * 128u * (max_pairs_per_expert <= 64 ? 64u : 128u) * 4u;
+}
 cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream);
 
 // Driver entry point for cuTensorMapEncodeTiled (resolved at run time).

@@ -98,22 +98,26 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   if (T == 0) return RIALLM_OK;
   if (!x || !out || !aligned16(x) || !aligned16(out)) return RIALLM_ERR_INVALID;
 
-  // The whole scratch layout of one bf16 block call must fit the array.
-  const rl::MoeLayout L = rl::moe_layout(T, H, I, E, k, RIALLM_DTYPE_BF16, 0);
-  if (L.total > kNoAllocScratchBytes) return RIALLM_ERR_MEMORY;
-
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return RIALLM_ERR_CUDA;
   DeviceSlot* slot = nullptr;
   if (int rc = device_setup(dev, &slot)) return rc;
 
+  // The whole scratch layout of one bf16 block call must fit the array;
+  // when the expert GEMM's split-tile workspace does not fit as well, the
+  // GEMM runs whole tiles per CTA instead.
+  rl::MoeLayout L = rl::moe_layout(T, H, I, E, k, RIALLM_DTYPE_BF16, 0, slot->num_sms);
+  if (L.total > kNoAllocScratchBytes) L = rl::moe_layout(T, H, I, E, k, RIALLM_DTYPE_BF16, 0, slot->num_sms, false);
+  if (L.total > kNoAllocScratchBytes) return RIALLM_ERR_MEMORY;
+
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* base = reinterpret_cast<char*>(slot->scratch);
   const int P = T * k;
-  // Only the status word must start at zero within the call; the router's
-  // completion counter (the layout's first slot) starts at zero with the
-  // array and the router resets it before it returns. Every other buffer is
-  // fully written before it is read within the call.
+  // Only the status word must be zeroed per call. The counters in the
+  // layout's first bytes (the router's completion counter, the expert
+  // GEMM's split-tile counters) start at zero with the array and every call
+  // returns them to zero. Every other buffer is fully written before it is
+  // read within the call.
   if (cudaMemsetAsync(slot->status, 0, sizeof(int), st) != cudaSuccess) return RIALLM_ERR_CUDA;
   int* topk_idx = reinterpret_cast<int*>(base + L.topk_idx);
   float* topk_w = reinterpret_cast<float*>(base + L.topk_w);
@@ -163,6 +167,8 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   g.ld_out = I;
   g.status = slot->status;
   g.max_pairs_per_expert = T;
+  g.sk_ws = L.sk_ws ? reinterpret_cast<float*>(base + L.sk_ws) : nullptr;
+  g.sk_flags = reinterpret_cast<int*>(base + L.sync + rl::kSkFlagsOffset);
   if (rl::launch_tc_gemm(g, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
   rl::TcGemmArgs d{};
   d.w = w->down_proj;
@@ -181,6 +187,8 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   d.ld_out = H;
   d.status = slot->status;
   d.max_pairs_per_expert = T;
+  d.sk_ws = L.sk_ws ? reinterpret_cast<float*>(base + L.sk_ws) : nullptr;
+  d.sk_flags = reinterpret_cast<int*>(base + L.sync + rl::kSkFlagsOffset);
   if (rl::launch_tc_gemm(d, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
   if (rl::launch_combine(reinterpret_cast<float*>(base + L.y_perm), inv, topk_idx, topk_w, T, k, H, nullptr,
                          nullptr, out, true, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st) != cudaSuccess)
