@@ -8,8 +8,8 @@
 // Data path per CTA (persistent, one per SM):
 //   producer warp     : TMA (128-byte swizzle, no multicast) of the packed
 //                       codes of two 128-row operands, 128 bytes per row per
-//                       stage, into a 3-deep shared-memory ring, plus L2
-//                       prefetches of the stages four ahead of that ring;
+//                       stage, into a shared-memory ring (4 stages deep when
+//                       every tile holds <= 64 pairs, else 3);
 //   token warp        : TMA of the bf16 token tiles (N x 128 K) of every A
 //                       stage into its own ring slot, so code prefetch
 //                       never waits on MMA progress;
@@ -23,36 +23,40 @@
 //                       memory, f32 accumulators in TMEM;
 //   4 epilogue warps  : tcgen05.ld of D0/D1 and either h = silu(D0)*D1
 //                       (gate_up, bf16 out) or plain f32 stores (down).
+// Measured on B200: packed bf16x2 FMA/SUB and LOP3 issue at half rate (one
+// warp instruction per 2 cycles per SM sub-partition), so the NF4 decode
+// (3 FMA-pipe instructions per 2 weights) is bound near 768 cycles per
+// 32768-weight stage; work is spread so that no other role competes.
+//
+// Scheduling: whole tiles round-robin over the CTAs while two or more full
+// waves remain, then stream-K shares of the rest (see Sched), so all SMs
+// stream the same number of weight bytes.
 //
 // NF4 scales and zero points ride in the same TMA stage as the codes (a
 // 128-row x 4-block box of each); 8-bit ones are fetched by the dequant
-// threads with cp.async, four stages ahead. NF4 follows the reference decode
-// exactly in its indexing: element 63 of a block uses the next block's scale
-// and zero (src/quantization.rs:55-72) -- for the stage's last block that is
-// the next stage's first, and for a row's last block the next row's first
-// block (loaded once per tile), or past the tensor's end scale 1 / zero 0.
+// threads with cp.async, a few stages ahead. NF4 follows the reference
+// decode exactly in its indexing: element 63 of a block uses the next
+// block's scale and zero (src/quantization.rs:55-72) -- for the stage's
+// last block that is the next stage's first (a global load at stage
+// start), for a row's last block the next row's first block, or past the
+// tensor's end scale 1 / zero 0.
 //
-// MMA issue: one tcgen05.mma occupies its issuing thread for ~160 cycles
-// whatever its N, while MMAs issued from different warps overlap. So four
-// issuer warps each own one accumulator when tiles are at most 64 pairs wide
-// (operand x K half: every sub-stage each issues the 2 K-steps of its half),
-// and two (one per operand) when tiles are 128 wide; the epilogue adds the
-// K halves.
-//
-// Issue cost matters as much: a tcgen05.commit or a barrier wait plus fence
-// costs an issuer about as much as an MMA, so the A ring is organised in
-// stages of 128 K (two 64-K sub-stages per operand) and the token producer
-// arrives on the same "full" barrier as the dequant warps (with its TMA
-// byte count): per stage an issuer does one wait, one fence, its MMAs and
-// one commit.
+// MMA issue: several issuer warps each own one accumulator, because MMAs
+// issued from different warps overlap: four when tiles are at most 64
+// pairs wide (operand x K half: every sub-stage each issues the 2 K-steps
+// of its half) and two (one per operand) when tiles are 128 wide; the
+// epilogue adds the K halves. A tcgen05.commit or a barrier wait plus
+// fence costs an issuer about as much as an MMA, so the A ring is organised
+// in stages of 128 K (two 64-K sub-stages per operand) and the token
+// producer arrives on the same "full" barrier as the dequant warps (with
+// its TMA byte count): per stage an issuer does one wait, one fence, its
+// MMAs (fully unrolled) and one commit.
 //
 // Tensor memory (512 columns): the accumulators from column 0 (4 x 32
 // when every tile of the launch holds at most 32 pairs, 4 x 64 for other
 // tiles of at most 64, 2 x 128 for wider ones), then a ring of A stages of
 // 128 columns each (operand 0 then operand 1; 64 columns = 128 bf16): three
-// stages behind 4 x 32 accumulators, two otherwise. The third stage lets
-// the dequant warps run a full stage ahead of MMA completion, which
-// matters most at decode sizes.
+// stages behind 4 x 32 accumulators, two otherwise.
 //
 // Every wait is bounded (common.cuh); on expiry the CTA raises an abort
 // flag, every role stops, in-flight copies and MMAs are drained with bounded
@@ -64,10 +68,9 @@
 namespace rl {
 namespace tc {
 
-constexpr int kRawStages = 3;
+constexpr int kRawStages = 4;                    // raw ring: 4 stages for narrow launches, 3 for wide
 constexpr int kBRegionBytes = 64 * 1024;         // token ring: 2 stages x 2 boxes x N x 128 B
 constexpr int kAStages = 3;                      // A ring: up to 3 stages of 128 K (4 x 64 K sub-stages)
-constexpr int kPrefetchStages = 4;              // raw stages prefetched into L2 ahead of the ring
 constexpr int kParamSlots = 6;                   // 8-bit parameter ring (cp.async)
 constexpr int kParamAhead = 4;                   // stages prefetched ahead
 constexpr int kNmax = 128;
@@ -84,8 +87,12 @@ constexpr uint32_t kTmemCols = 512;
 constexpr int kMaxE = 256;
 
 constexpr int kSmemRaw = 0;
-constexpr int kSmemB = kSmemRaw + kRawStages * kRawStageBytes;
-constexpr int kSmemPrm = kSmemB + kBRegionBytes;
+// The token ring follows the raw ring: at 4 x 40 KiB for narrow launches
+// (3 token stages of <= 16 KiB), at 3 x 40 KiB for wide ones (2 of 32 KiB).
+constexpr int kNarrowBBytes = 3 * 2 * 64 * 128;
+constexpr int kSmemPrm = (kRawStages * kRawStageBytes + kNarrowBBytes) > ((kRawStages - 1) * kRawStageBytes + kBRegionBytes)
+                             ? kRawStages * kRawStageBytes + kNarrowBBytes
+                             : (kRawStages - 1) * kRawStageBytes + kBRegionBytes;
 constexpr int kSmemBar = kSmemPrm + kParamSlots * 256 * 2 * 4;
 constexpr int kNumBars = 2 * kRawStages + 2 * kAStages + 2 + kMmaWarps;
 constexpr int kSmemMisc = kSmemBar + 8 * 40;
@@ -338,6 +345,21 @@ __device__ __forceinline__ void dequant_int8_half(const uint4 a4, const uint4 b4
   }
 }
 
+// One A stage of MMAs for one issuer: sub-stages u = 0, 1 (64 K each) and
+// K steps kk0 .. kk0 + NKK - 1 of each, accumulating into d (the item's
+// first MMA overwrites).
+template <int NKK>
+__device__ __forceinline__ void issue_stage(uint32_t d, uint32_t a_k, uint64_t b0_k, uint64_t b1_k,
+                                            uint32_t idesc, bool first) {
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+#pragma unroll
+    for (int i = 0; i < NKK; ++i)
+      tc_mma_ts(d, a_k + u * 32 + i * 8, (u ? b1_k : b0_k) + (uint64_t)(i * 2), idesc,
+                (first && u == 0 && i == 0) ? 0u : 1u);
+  }
+}
+
 template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tm_raw,
@@ -356,7 +378,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint8_t* raw = smem + kSmemRaw;
-  uint8_t* bst = smem + kSmemB;
+  // Narrow launches (every tile <= 64 pairs): 4 issuers, accumulator of
+  // issuer j = (operand j&1, K half j>>1) at column acc_cols j. Wide
+  // launches: 2 issuers, accumulator of operand j at column 128 j.
+  const bool narrow = p.d_cols == 64;
+  const int n_rs = narrow ? kRawStages : kRawStages - 1;  // raw ring depth
+  uint8_t* bst = smem + n_rs * kRawStageBytes;
   float* prm = reinterpret_cast<float*>(smem + kSmemPrm);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kSmemBar);
   uint64_t* raw_full = bars;
@@ -375,10 +402,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* off_s = cnt_s + kMaxE;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Narrow launches (every tile <= 64 pairs): 4 issuers, accumulator of
-  // issuer j = (operand j&1, K half j>>1) at column 64 j. Wide launches:
-  // 2 issuers, accumulator of operand j at column 128 j.
-  const bool narrow = p.d_cols == 64;
   const int n_iss = narrow ? 4 : 2;
   const uint32_t b_box = narrow ? 64u * 128u : 128u * 128u;  // one 64-K token box
   const uint32_t b_stage = 2 * b_box;
@@ -453,38 +476,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------- producer: codes (+ NF4 params)
     if (lane == 0) {
       uint32_t it = 0;
+      RingPos rr;
       bool ok = true;
       const uint32_t stage_bytes = kNF4 ? (uint32_t)kRawStageBytes : (uint32_t)(2 * kRawOpBytes);
       Sched sc;
       sc.init(sk, total, n_raw);
-      // L2 prefetch cursor, kPrefetchStages raw stages ahead of the loads:
-      // keeps more HBM reads in flight than the shared-memory ring holds.
-      Sched ps = sc;
-      Item pi;
-      bool pv = sched_next(ps, pi, tile_start, ntn, cnt_s, off_s, p);
-      int pc = pv ? pi.r0 : 0;
-      auto prefetch_next = [&]() {
-        if (!pv) return;
-        tma_prefetch_l2_2d(&tm_raw, pc * 128, pi.ti.row0);
-        tma_prefetch_l2_2d(&tm_raw, pc * 128, pi.ti.row1);
-        if (kNF4) {
-          tma_prefetch_l2_2d(&tm_scl, pc * PPS, pi.ti.row0);
-          tma_prefetch_l2_2d(&tm_zer, pc * PPS, pi.ti.row0);
-          tma_prefetch_l2_2d(&tm_scl, pc * PPS, pi.ti.row1);
-          tma_prefetch_l2_2d(&tm_zer, pc * PPS, pi.ti.row1);
-        }
-        if (++pc == pi.r1) {
-          pv = sched_next(ps, pi, tile_start, ntn, cnt_s, off_s, p);
-          if (pv) pc = pi.r0;
-        }
-      };
-      for (int i = 0; i < kPrefetchStages; ++i) prefetch_next();
       Item im;
       while (ok && sched_next(sc, im, tile_start, ntn, cnt_s, off_s, p)) {
-        for (int c = im.r0; c < im.r1; ++c, ++it) {
-          prefetch_next();
-          const int s = it % kRawStages;
-          if (!mbar_wait(&raw_empty[s], ((it / kRawStages) & 1) ^ 1, abort_s, p.status)) {
+        for (int c = im.r0; c < im.r1; ++c, ++it, rr.next(n_rs)) {
+          const int s = rr.s;
+          if (!mbar_wait(&raw_empty[s], rr.ph ^ 1, abort_s, p.status)) {
             ok = false;
             break;
           }
@@ -502,8 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Drain: every issued copy lands before the CTA can exit.
-      for (uint32_t j = (it > (uint32_t)kRawStages ? it - kRawStages : 0); j < it; ++j)
-        wait_drain(&raw_full[j % kRawStages], (j / kRawStages) & 1);
+      for (uint32_t j = (it > (uint32_t)n_rs ? it - n_rs : 0); j < it; ++j)
+        wait_drain(&raw_full[j % n_rs], (j / n_rs) & 1);
     }
   } else if (warp == kWarpBProd) {
     // ---------------------------------------------- token tile producer
@@ -540,7 +541,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && j < n_iss) {
       const int op = narrow ? (j & 1) : j;        // operand: 0 gate / rows r, 1 up / rows r+128
       const int kk0 = narrow ? 2 * (j >> 1) : 0;  // first K step of this issuer in a sub-stage
-      const int nkk = narrow ? 2 : 4;
       const uint32_t d_col = acc_cols * j;
       RingPos rp;
       uint32_t tit = 0;
@@ -559,18 +559,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_st = tmem + col_a + s * 128 + op * 64;
-          const uint64_t bdesc0 = sdesc_kmajor_sw128(smem_u32(bst + s * b_stage));
-          const uint64_t bdesc1 = sdesc_kmajor_sw128(smem_u32(bst + s * b_stage + b_box));
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const uint64_t bdesc = u ? bdesc1 : bdesc0;
-            for (int i = 0; i < nkk; ++i) {
-              const int kk = kk0 + i;
-              tc_mma_ts(tmem + d_col, a_st + u * 32 + kk * 8, bdesc + (uint64_t)(kk * 2), idesc,
-                        ((as - as0) | u | i) ? 1u : 0u);
-            }
-          }
+          const uint32_t a_k = tmem + col_a + s * 128 + op * 64 + kk0 * 8;
+          const uint64_t b0_k = sdesc_kmajor_sw128(smem_u32(bst + s * b_stage)) + (uint64_t)(kk0 * 2);
+          const uint64_t b1_k = sdesc_kmajor_sw128(smem_u32(bst + s * b_stage + b_box)) + (uint64_t)(kk0 * 2);
+          if (narrow)
+            issue_stage<2>(tmem + d_col, a_k, b0_k, b1_k, idesc, as == as0);
+          else
+            issue_stage<4>(tmem + d_col, a_k, b0_k, b1_k, idesc, as == as0);
           issued = true;
           tc_commit(&empty[s]);
         }
@@ -592,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int pt = dw * 32 + lane;        // 8-bit parameter slot owner 0..255
     const int swz = r & 7;
     uint32_t rit = 0;
-    RingPos rp;
+    RingPos rp, rr;
     bool ok = true;
     const uint64_t blocks_per_row = (uint64_t)(p.K / BS);
     Sched sc;
@@ -609,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           cp_async_commit();
         }
       }
-      for (int c = im.r0; c < im.r1; ++c, ++rit) {
+      for (int c = im.r0; c < im.r1; ++c, ++rit, rr.next(n_rs)) {
         // NF4: element 63 of the stage's last block takes the parameters of
         // the block after it -- the next stage's first, the next row's first
         // for the row's last stage, or 1.0 / 0.0 past the tensor's end.
@@ -625,8 +620,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           cp_async_commit();
           cp_async_wait<kParamAhead>();
         }
-        const int rs = rit % kRawStages;
-        if (!warp_wait(&raw_full[rs], (rit / kRawStages) & 1, abort_s, p.status)) {
+        const int rs = rr.s;
+        if (!warp_wait(&raw_full[rs], rr.ph, abort_s, p.status)) {
           ok = false;
           break;
         }
@@ -808,7 +803,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int jj = 0; jj < 8; ++jj) {
             if (n0 + jj < ti.nv) {
               const float gv = __uint_as_float(g[jj]), uv = __uint_as_float(u[jj]);
-              const float hv = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv);
+              const float hv = __fdividef(gv, 1.0f + __expf(-gv)) * uv;
               const __nv_bfloat16 hb = __float2bfloat16_rn(hv);
               p.h_out[(uint64_t)(ti.pos0 + n0 + jj) * p.ld_out + col] = *reinterpret_cast<const uint16_t*>(&hb);
             }
