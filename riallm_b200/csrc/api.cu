@@ -465,7 +465,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
   {
     PhaseScope ps(ctx, st, RIALLM_PHASE_ROUTE);
     if (int s = route_into(ctx, w->gate, x, T, H, E, k, bf16, base, L, st)) return s;
-    ctx->launches += 3;
+    ctx->launches += 1;
   }
   const int* counts = (const int*)(base + L.counts);
   const int* offsets = (const int*)(base + L.offsets);
@@ -498,6 +498,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     g.max_pairs_per_expert = T;
     g.sk_ws = L.sk_ws ? (float*)(base + L.sk_ws) : nullptr;
     g.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
+    g.pdl = true;  // follows the gather
     {
       PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
       RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
@@ -522,6 +523,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     d.max_pairs_per_expert = T;
     d.sk_ws = L.sk_ws ? (float*)(base + L.sk_ws) : nullptr;
     d.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
+    d.pdl = true;  // follows the gate_up GEMM
     {
       PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
       RL_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");

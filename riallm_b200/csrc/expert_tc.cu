@@ -402,6 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   int* off_s = cnt_s + kMaxE;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // The next expert GEMM may queue now; its CTAs take SMs as these exit.
+  pdl_launch_dependents();
   const int n_iss = narrow ? 4 : 2;
   const uint32_t b_box = narrow ? 64u * 128u : 128u * 128u;  // one 64-K token box
   const uint32_t b_stage = 2 * b_box;
@@ -515,6 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       Sched sc;
       sc.init(sk, total, n_raw);
       Item im;
+      pdl_wait();  // token tiles are the previous kernel's output
       while (ok && sched_next(sc, im, tile_start, ntn, cnt_s, off_s, p)) {
         const Tile& ti = im.ti;
         const CUtensorMap* tm = ti.N == 16 ? &tm_b16 : ti.N == 32 ? &tm_b32 : ti.N == 64 ? &tm_b64 : &tm_b128;
@@ -716,6 +719,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     cp_async_wait<0>();
   } else {
     // ------------------------------------------------------- epilogue
+    // Outputs and the split-tile workspace may still be in use by the
+    // previous kernel until it completes.
+    pdl_wait();
     const int q = warp & 3;
     const int m = 32 * q + lane;
     const uint64_t G = gridDim.x;
@@ -897,8 +903,18 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
     if (err != cudaSuccess) return err;
     done = true;
   }
-  kern<<<num_sms, tc::kThreads, tc::kSmemBytes, stream>>>(tm_raw, tm_scl, tm_zer, tm_b[0], tm_b[1], tm_b[2],
-                                                         tm_b[3], p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms);
+  cfg.blockDim = dim3(tc::kThreads);
+  cfg.dynamicSmemBytes = tc::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tm_raw, tm_scl, tm_zer, tm_b[0], tm_b[1], tm_b[2], tm_b[3], p);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

@@ -136,6 +136,11 @@ struct TcGemmArgs {
   int max_pairs_per_expert;  // upper bound on any expert's pair count (<= T)
   float* sk_ws;              // split-tile partial sums, tc_sk_ws_bytes(); null: whole tiles per CTA
   int* sk_flags;             // num_sms counters, zero between launches
+  // Launch with programmatic stream serialization: the prologue and the
+  // weight stream may start while the previous kernel (which must not
+  // produce the routing counts) is still running; token tiles, outputs and
+  // the split-tile workspace are touched only after griddepcontrol.wait.
+  bool pdl;
 };
 // Bytes of the split-tile workspace of launch_tc_gemm: one slot of
 // 2 operands x 128 rows x (64 or 128) f32 columns per CTA (= per SM).

@@ -169,6 +169,7 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   g.max_pairs_per_expert = T;
   g.sk_ws = L.sk_ws ? reinterpret_cast<float*>(base + L.sk_ws) : nullptr;
   g.sk_flags = reinterpret_cast<int*>(base + L.sync + rl::kSkFlagsOffset);
+  g.pdl = true;  // follows the gather
   if (rl::launch_tc_gemm(g, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
   rl::TcGemmArgs d{};
   d.w = w->down_proj;
@@ -189,6 +190,7 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   d.max_pairs_per_expert = T;
   d.sk_ws = L.sk_ws ? reinterpret_cast<float*>(base + L.sk_ws) : nullptr;
   d.sk_flags = reinterpret_cast<int*>(base + L.sync + rl::kSkFlagsOffset);
+  d.pdl = true;  // follows the gate_up GEMM
   if (rl::launch_tc_gemm(d, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
   if (rl::launch_combine(reinterpret_cast<float*>(base + L.y_perm), inv, topk_idx, topk_w, T, k, H, nullptr,
                          nullptr, out, true, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st) != cudaSuccess)

@@ -250,6 +250,9 @@ cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stre
 __global__ void __launch_bounds__(256) gather_kernel(const void* __restrict__ x, int x_bf16,
                                                      const int* __restrict__ perm_pair, int k, int H,
                                                      void* __restrict__ x_perm, int pair_perm) {
+  // The expert GEMM that follows reads only the routing counts (final
+  // before this kernel started) until it waits for x_perm, so it may start.
+  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int esz = x_bf16 ? 2 : 4;
   const int n16 = H * esz / 16;
