@@ -103,6 +103,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) accesses of the CTA's shared memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // ------------------------------------------- programmatic dependent launch
 
 // Lets the next kernel of the stream, when launched with programmatic

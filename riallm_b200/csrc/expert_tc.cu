@@ -646,6 +646,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           sc8 = sl[0];
           ze8 = sl[1];
         }
+        // NF4: the next sub-stage's codes are loaded one sub-stage ahead.
+        uint4 pc0 = make_uint4(0, 0, 0, 0), pc1 = pc0;
+        if (kNF4) {
+          pc0 = *reinterpret_cast<const uint4*>(rowp + ((0 ^ swz) << 4));
+          pc1 = *reinterpret_cast<const uint4*>(rowp + ((1 ^ swz) << 4));
+        }
 #pragma unroll
         for (int v = 0; v < AS_PER_RAW; ++v, rp.next(n_ring)) {
           const int s = rp.s;
@@ -655,8 +661,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int uu = 0; uu < 2; ++uu) {
             const int u = 2 * v + uu;  // 64-K sub-stage inside the raw stage
             if (kNF4) {
-              const uint4 c0 = *reinterpret_cast<const uint4*>(rowp + (((2 * u) ^ swz) << 4));
-              const uint4 c1 = *reinterpret_cast<const uint4*>(rowp + (((2 * u + 1) ^ swz) << 4));
+              const uint4 c0 = pc0, c1 = pc1;
+              if (u < 3) {
+                pc0 = *reinterpret_cast<const uint4*>(rowp + (((2 * u + 2) ^ swz) << 4));
+                pc1 = *reinterpret_cast<const uint4*>(rowp + (((2 * u + 3) ^ swz) << 4));
+              }
               // Block u's constants in both halves, and (block u, block u+1)
               // for the register holding element 63.
               const Bf16Pair& Pc = (u < 2) ? P01 : P23;
