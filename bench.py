@@ -178,7 +178,7 @@ def config_dict(args, world):
     return {"workload": f"mixtral8x7b_moe_block_nf4_decode_T{args.tokens}",
             "hidden": H, "intermediate": I, "experts": E, "top_k": TOP_K,
             "tokens_per_step_per_gpu": args.tokens, "compression": "FourBit (riallm NF4 layout)",
-            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "parallelism": f"ep{world} (expert-parallel: {E // max(world, 1)} experts per GPU, tokens all-gathered, partials reduce-scattered over NCCL)" if world > 1 else "single",
             "l2_policy": "inputs larger than L2 (880.8 MB of NF4 weights per step vs 126 MB L2)"}
 
 
@@ -308,12 +308,18 @@ def run_ours(args, rank, world, local):
     hbm_peak, bf16_peak, bf16_sust, peak_src = load_peaks()
 
     d = make_layer(rb, torch, device)
+    if world > 1:
+        return run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_src)
     blk = Block(rb, torch, d, args.tokens, device)
     U = blk.distinct_experts()
 
     # Capture one step in a CUDA graph (after a warm-up that sizes the arena).
     for _ in range(3):
         blk()
+    torch.cuda.synchronize()
+    l0 = blk.ctx.launch_count()
+    blk()
+    launches_per_step = blk.ctx.launch_count() - l0  # kernels of one step, counted by the library
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
@@ -325,8 +331,7 @@ def run_ours(args, rank, world, local):
     launches0 = blk.ctx.launch_count()
     with ClockSampler(local) as clk:
         ms = timed(torch, g.replay, args.steps, args.warmup, dist, world)
-    per_step_launches = (blk.ctx.launch_count() - launches0)  # captured launches are counted once
-    launches_per_step = 7
+    per_step_launches = (blk.ctx.launch_count() - launches0)  # graph replays launch nothing through the library
     ms_per_step = ms / args.steps
     value = world * args.tokens * args.steps / (ms / 1000.0)
 
@@ -403,7 +408,7 @@ def run_ours(args, rank, world, local):
             "config": config_dict(args, world),
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
-            "gpu_launches_note": "7 kernels per step replayed from one CUDA graph (route 3, gather 1, expert GEMMs 2, combine 1)",
+            "gpu_launches_note": f"{launches_per_step} kernels per step (router, gather, expert gate_up and down GEMMs, combine) replayed from one CUDA graph",
             "captured_launches": per_step_launches,
             "clocks": clk.summary(), "sweep": sweep,
         }
@@ -412,6 +417,94 @@ def run_ours(args, rank, world, local):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_src):
+    """Expert parallel over `world` GPUs (weak scaling: args.tokens tokens per
+    GPU). Rank r keeps experts [r E/W, (r+1) E/W); a step all-gathers the
+    tokens, runs the local experts for all of them (riallm_cuda_moe_forward_ep)
+    and reduce-scatters the float32 partials (riallm_b200.ep)."""
+    from riallm_b200.ep import ExpertParallelMoE, expert_range
+    e_b, e_l = expert_range(E, rank, world)
+    local_w = {"mlp.gate.weight": d["mlp.gate.weight"],
+               "mlp.experts.gate_up_proj": d["mlp.experts.gate_up_proj"].expert_slice(e_b, e_l),
+               "mlp.experts.down_proj": d["mlp.experts.down_proj"].expert_slice(e_b, e_l)}
+    blk = ExpertParallelMoE(local_w, E, TOP_K)
+    gen = torch.Generator(device=device).manual_seed(1000 + args.tokens + 7919 * rank)
+    x = torch.empty(args.tokens, H, device=device).normal_(0, 1, generator=gen).to(torch.bfloat16)
+    ctx = rb.Context.get(device.index or 0)
+    ctx.reserve(world * args.tokens, H, I, E, TOP_K, torch.bfloat16)
+    out = None
+
+    def step():
+        nonlocal out
+        out = blk(x)
+    step()
+    l0 = ctx.launch_count()
+    step()
+    launches_per_step = ctx.launch_count() - l0  # library kernels of one step
+    with ClockSampler(local) as clk:
+        ms = timed(torch, step, args.steps, args.warmup, dist, world)
+    ms_per_step = ms / args.steps
+    value = world * args.tokens * args.steps / (ms / 1000.0)
+
+    # Local expert GEMM phases on this rank (roofline of the dominant kernel).
+    torch.cuda.synchronize()
+    ctx.profile(True)
+    torch.cuda._sleep(int(2e8))
+    for _ in range(10):
+        step()
+    torch.cuda.synchronize()
+    ctx.profile(False)
+    ph, calls = ctx.profile_read()
+    ph = {k: v / max(calls, 1) for k, v in ph.items()}
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x)
+    _, _, counts, _, _ = rb.route(d["mlp.gate.weight"], torch.cat(parts, 0), TOP_K, E)
+    U_local = int((counts[e_b:e_b + e_l] > 0).sum().item())
+    P_local = int(counts[e_b:e_b + e_l].sum().item())
+    kern_ms = ph["gate_up"] + ph["down"]
+    bytes_step = U_local * BYTES_PER_EXPERT + P_local * (H * 2 + 2 * I * 2 + H * 4)
+    achieved = bytes_step / (kern_ms / 1000.0) / 1e9 if kern_ms > 0 else 0.0
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                "kernel": "expert_gemm_kernel<NF4> (rank 0's gate_up + down launches of one step)",
+                "algorithmic_bytes_per_step": bytes_step, "distinct_experts": U_local,
+                "kernel_ms_per_step": round(kern_ms, 4),
+                "phase_ms_per_step": {k: round(v, 4) for k, v in ph.items()},
+                "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src}
+
+    # End to end: this rank's tokens from pinned host memory, the block, the
+    # output back to the host, every step.
+    hx = torch.empty_like(x, device="cpu").pin_memory()
+    hx.copy_(x.cpu())
+    hout = torch.empty_like(hx).pin_memory()
+
+    def e2e_step():
+        x.copy_(hx, non_blocking=True)
+        step()
+        hout.copy_(out, non_blocking=True)
+    e2e_ms = timed(torch, e2e_step, args.steps, args.warmup, dist, world)
+    nbytes = x.numel() * 2
+    e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
+           "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
+           "ms_per_step": round(e2e_ms / args.steps, 4)}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,0.02) weights (torch cuda generator, seed 2) NF4-quantized; N(0,1) bf16 activations",
+            "config": config_dict(args, world),
+            "roofline": roofline, "cpu_baseline": None, "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches_note": f"{launches_per_step} library kernels per step per GPU (router, gather, expert gate_up and down GEMMs, partial combine) plus NCCL all-gather and reduce-scatter",
+            "clocks": clk.summary(), "sweep": [],
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
     return 0
 
 

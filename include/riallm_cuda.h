@@ -154,6 +154,23 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w,
                                 int32_t I, int32_t E, int32_t k,
                                 int32_t act_dtype, uint32_t flags, void* stream);
 
+/* No counterpart in the reference (it has no multi-GPU path). One rank's
+ * share of an expert-parallel MoE block: rank r of W owns the experts
+ * [e_begin, e_begin + e_local). x holds the bf16 tokens of every rank
+ * ([T,H], gathered by the caller), w->gate the full router [E,H], and
+ * w->gate_up_proj / w->down_proj only the owned experts ([e_local,2I,H] and
+ * [e_local,H,I]). Every token is routed over all E experts exactly as by
+ * riallm_cuda_moe_forward; partial [T,H] (float32) receives, per token, the
+ * routing-weighted sum of its owned experts' outputs in expert-ascending
+ * order (0 where it has none). Summing the W partials (a reduce-scatter)
+ * and rounding to bf16 gives riallm_cuda_moe_forward's output up to float32
+ * summation order inside the expert GEMMs (their K ranges are split across
+ * SMs differently when a rank holds fewer experts). Routed experts only. */
+int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
+                                   const void* x, float* partial, int32_t T,
+                                   int32_t H, int32_t I, int32_t E, int32_t k,
+                                   int32_t e_begin, int32_t e_local, void* stream);
+
 /* Grows the context's scratch arena for blocks up to these sizes now, so
  * that later riallm_cuda_moe_forward calls allocate nothing. */
 int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I,

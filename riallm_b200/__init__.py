@@ -114,6 +114,8 @@ SIGNATURES = {
     "riallm_cuda_launch_count": (_u64, [_vp]),
     "riallm_cuda_moe_forward_noalloc": (_i32, [ctypes.POINTER(CMoeWeights), _vp, _vp, _i32, _i32, _i32,
                                                _i32, _i32, _u32, _vp]),
+    "riallm_cuda_moe_forward_ep": (_i32, [_vp, ctypes.POINTER(CMoeWeights), _vp, _vp, _i32, _i32, _i32,
+                                          _i32, _i32, _i32, _i32, _vp]),
 }
 
 PHASES = ("route", "gather", "gate_up", "down", "shared", "combine")
@@ -303,6 +305,30 @@ class QuantizedTensor:
     def nbytes(self) -> int:
         return self.data.numel() * self.data.element_size() + 4 * (self.scales.numel() + self.zero_points.numel())
 
+    def expert_slice(self, e_begin: int, e_count: int) -> "QuantizedTensor":
+        """Experts [e_begin, e_begin + e_count) of a quantized [E, ...] expert
+        tensor, as views (no copy). Blocks never straddle experts, so the
+        slice is a contiguous range of codes, scales and zero points; the
+        parameters of the block after the slice ride along, because the
+        reference's NF4 decode gives the last element of every block the
+        next block's scale and zero (src/quantization.rs:55-72), and for the
+        slice's last block that block belongs to the next expert."""
+        if self.qtype == CompressionType.None_:
+            raise QuantizationError("expert_slice expects a quantized tensor")
+        E = int(self.shape[0])
+        if e_begin < 0 or e_count <= 0 or e_begin + e_count > E:
+            raise ConfigError(f"expert range [{e_begin}, {e_begin + e_count}) outside [0, {E})")
+        per = self.numel // E
+        bpe = per // self.block_size
+        if per % self.block_size:
+            raise QuantizationError("expert size is not a whole number of quantization blocks")
+        bytes_per = per // 2 if self.qtype == CompressionType.FourBit else per
+        b0, b1 = e_begin * bpe, (e_begin + e_count) * bpe
+        extra = 1 if b1 < self.scales.numel() else 0
+        return QuantizedTensor(self.data[e_begin * bytes_per:(e_begin + e_count) * bytes_per],
+                               (e_count,) + tuple(self.shape[1:]), self.qtype,
+                               self.scales[b0:b1 + extra], self.zero_points[b0:b1 + extra], self.block_size)
+
 
 def quantize_tensor(tensor: torch.Tensor, compression: CompressionType) -> QuantizedTensor:
     """src/quantization.rs:99-107 (NF4 :111-176, 8-bit :199-245), on the GPU,
@@ -423,6 +449,32 @@ def apply_moe(tensors: Mapping[str, TensorLike], hidden: torch.Tensor, num_exper
                                             1 if add_to_out else 0, _stream_ptr(flat)))
     del keep
     return out.view(shape)
+
+
+def apply_moe_ep_partial(tensors: Mapping[str, TensorLike], hidden: torch.Tensor, num_experts_per_tok: int,
+                         num_experts: int, e_begin: int, e_local: int,
+                         ctx: Optional[Context] = None) -> torch.Tensor:
+    """One expert-parallel rank's share of the MoE block (no counterpart in
+    the reference, which has no multi-GPU path): hidden [T,H] bf16 holds the
+    tokens of every rank, "mlp.gate.weight" the full router, the expert
+    tensors only experts [e_begin, e_begin + e_local) (see
+    QuantizedTensor.expert_slice). Returns float32 [T,H]: per token, the
+    routing-weighted sum of its owned experts' outputs in expert-ascending
+    order; the sum of all ranks' partials is the block output."""
+    if not hidden.is_cuda or hidden.dtype != torch.bfloat16:
+        raise ConfigError("hidden must be a bf16 CUDA tensor")
+    w, keep, gu = _weights(tensors)
+    H = int(hidden.shape[-1])
+    flat = hidden.reshape(-1, H).contiguous()
+    T = flat.shape[0]
+    I = int(gu.shape[1]) // 2 if len(gu.shape) == 3 else gu.numel // (2 * int(e_local) * H)
+    partial = torch.empty((T, H), dtype=torch.float32, device=flat.device)
+    ctx = ctx or Context.get(hidden.device.index or 0)
+    ctx.check(lib().riallm_cuda_moe_forward_ep(ctx.ptr, ctypes.byref(w), flat.data_ptr(), partial.data_ptr(),
+                                               T, H, I, int(num_experts), int(num_experts_per_tok),
+                                               int(e_begin), int(e_local), _stream_ptr(flat)))
+    del keep
+    return partial
 
 
 def route(gate: TensorLike, hidden: torch.Tensor, num_experts_per_tok: int, num_experts: int,

@@ -628,6 +628,101 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
   return RIALLM_OK;
 }
 
+int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x,
+                                   float* partial, int32_t T, int32_t H, int32_t I, int32_t E, int32_t k,
+                                   int32_t e_begin, int32_t e_local, void* stream) {
+  if (!ctx || !w) return RIALLM_ERR_INVALID;
+  if ((!x || !partial) && T != 0) return set_err(ctx, RIALLM_ERR_INVALID, "null x/partial");
+  if (int s = check_shapes(ctx, T, H, I, E, k)) return s;
+  if (e_begin < 0 || e_local <= 0 || e_begin + e_local > E)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "expert range [e_begin, e_begin + e_local) outside [0, E)");
+  if (w->shared_gate_proj.data != nullptr)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "expert-parallel calls take routed experts only");
+  if (int s = check_qtensor(ctx, w->gate, (uint64_t)E * H, "mlp.gate.weight", false)) return s;
+  if (int s = check_qtensor(ctx, w->gate_up_proj, (uint64_t)e_local * 2 * I * H, "mlp.experts.gate_up_proj", true))
+    return s;
+  if (int s = check_qtensor(ctx, w->down_proj, (uint64_t)e_local * H * I, "mlp.experts.down_proj", true)) return s;
+  if (T == 0) return RIALLM_OK;
+  if (!aligned16(x) || !aligned16(partial)) return set_err(ctx, RIALLM_ERR_INVALID, "x/partial must be 16-byte aligned");
+  if (int s = set_device(ctx)) return s;
+  const int P = T * k;
+  MoeLayout L = rl::moe_layout(T, H, I, E, k, RIALLM_DTYPE_BF16, 0, ctx->num_sms);
+  if (int s = ensure_arena(ctx, L.total)) return s;
+  char* base = (char*)ctx->arena;
+  cudaStream_t st = (cudaStream_t)stream;
+  {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_ROUTE);
+    if (int s = route_into(ctx, w->gate, x, T, H, E, k, true, base, L, st)) return s;
+    ctx->launches += 1;
+  }
+  // This rank's experts own the pair rows [offsets[e_begin], offsets[e_end]).
+  const int* counts = (const int*)(base + L.counts) + e_begin;
+  const int* offsets = (const int*)(base + L.offsets) + e_begin;
+  {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_GATHER);
+    RL_CUDA(ctx, rl::launch_gather(x, true, (const int*)(base + L.perm_pair), k, P, H, base + L.x_perm,
+                                   w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st, offsets,
+                                   offsets + e_local),
+            "gather");
+    ctx->launches += 1;
+  }
+  rl::TcGemmArgs g{};
+  g.w = w->gate_up_proj;
+  g.K = H;
+  g.rows_per_expert = 2 * I;
+  g.a1_offset = I;
+  g.m_step = 128;
+  g.m_tiles = I / 128;
+  g.b = base + L.x_perm;
+  g.P = P;
+  g.counts = counts;
+  g.offsets = offsets;
+  g.E = e_local;
+  g.swiglu = true;
+  g.h_pair_perm = w->down_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT;
+  g.h_out = (uint16_t*)(base + L.h_perm);
+  g.ld_out = I;
+  g.status = ctx->d_status;
+  g.max_pairs_per_expert = T;
+  g.sk_ws = L.sk_ws ? (float*)(base + L.sk_ws) : nullptr;
+  g.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
+  g.pdl = true;  // follows the gather
+  {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
+    RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
+    ctx->launches += 1;
+  }
+  rl::TcGemmArgs d = g;
+  d.w = w->down_proj;
+  d.K = I;
+  d.rows_per_expert = H;
+  d.a1_offset = 128;
+  d.m_step = 256;
+  d.m_tiles = H / 256;
+  d.b = base + L.h_perm;
+  d.swiglu = false;
+  d.h_pair_perm = false;
+  d.h_out = nullptr;
+  d.y_out = (float*)(base + L.y_perm);
+  d.ld_out = H;
+  d.pdl = true;  // follows the gate_up GEMM
+  {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
+    RL_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");
+    ctx->launches += 1;
+  }
+  {
+    PhaseScope ps(ctx, st, RIALLM_PHASE_COMBINE);
+    RL_CUDA(ctx, rl::launch_combine((const float*)(base + L.y_perm), (const int*)(base + L.inv_pos),
+                                    (const int*)(base + L.topk_idx), (const float*)(base + L.topk_w), T, k, H,
+                                    nullptr, nullptr, partial, false, false, st, e_begin, e_begin + e_local),
+            "combine (partial)");
+    ctx->launches += 1;
+  }
+  if (ctx->profiling) ctx->profiled_calls += 1;
+  return RIALLM_OK;
+}
+
 int32_t riallm_cuda_profile_enable(riallm_ctx* ctx, int32_t enable) {
   if (!ctx) return RIALLM_ERR_INVALID;
   ctx->profiling = enable != 0;

@@ -80,14 +80,19 @@ cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stre
 // Gathers token rows into expert-sorted pair order. pair_perm (bf16 only)
 // stores each group of 8 columns in the K order of the NF4 tensor-core
 // decode: [0,4,1,5,2,6,3,7].
+// row_begin / row_end (device ints, optional): only rows [*row_begin,
+// *row_end) are written (an expert-parallel rank's experts).
 cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int k, int P, int H,
-                          void* x_perm, bool pair_perm, cudaStream_t stream);
+                          void* x_perm, bool pair_perm, cudaStream_t stream,
+                          const int* row_begin = nullptr, const int* row_end = nullptr);
 // out[t] = sum over t's pairs in expert-ascending order of w * y_perm[pos]
 // (+ shared expert), optional residual add, cast to the activation dtype.
+// Pairs whose expert lies outside [e_begin, e_end) are skipped.
 cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* topk_idx,
                            const float* topk_w, int T, int k, int H, const float* shared_y,
                            const float* shared_gate, void* out, bool out_bf16, bool add_to_out,
-                           cudaStream_t stream);
+                           cudaStream_t stream, int e_begin = 0,
+                           int e_end = 1 << 30);
 
 // Generic CUDA-core grouped GEMM with on-the-fly dequant (float32 path and
 // the shared expert): Y[pos, r] = sum_c X[pos, c] * W[row_base(e) + r, c].

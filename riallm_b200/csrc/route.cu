@@ -249,11 +249,15 @@ cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stre
 // Row blockIdx.x of x_perm, 16-byte chunks blockIdx.y * 256 + threadIdx.x.
 __global__ void __launch_bounds__(256) gather_kernel(const void* __restrict__ x, int x_bf16,
                                                      const int* __restrict__ perm_pair, int k, int H,
-                                                     void* __restrict__ x_perm, int pair_perm) {
+                                                     void* __restrict__ x_perm, int pair_perm,
+                                                     const int* __restrict__ row_begin,
+                                                     const int* __restrict__ row_end) {
   // The expert GEMM that follows reads only the routing counts (final
   // before this kernel started) until it waits for x_perm, so it may start.
   pdl_launch_dependents();
   const int row = blockIdx.x;
+  // Expert-parallel calls gather only the rows of this rank's experts.
+  if (row_begin && (row < __ldg(row_begin) || row >= __ldg(row_end))) return;
   const int esz = x_bf16 ? 2 : 4;
   const int n16 = H * esz / 16;
   const int i = blockIdx.y * blockDim.x + threadIdx.x;
@@ -275,12 +279,13 @@ __global__ void __launch_bounds__(256) gather_kernel(const void* __restrict__ x,
 }
 
 cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int k, int P, int H,
-                          void* x_perm, bool pair_perm, cudaStream_t stream) {
+                          void* x_perm, bool pair_perm, cudaStream_t stream, const int* row_begin,
+                          const int* row_end) {
   if (P == 0) return cudaSuccess;
   const int n16 = H * (x_bf16 ? 2 : 4) / 16;
   const dim3 grid(P, (n16 + 255) / 256);
   gather_kernel<<<grid, 256, 0, stream>>>(x, x_bf16 ? 1 : 0, perm_pair, k, H, x_perm,
-                                          (pair_perm && x_bf16) ? 1 : 0);
+                                          (pair_perm && x_bf16) ? 1 : 0, row_begin, row_end);
   return cudaGetLastError();
 }
 
@@ -291,7 +296,7 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
                                const int* __restrict__ topk_idx, const float* __restrict__ topk_w,
                                int k, int H, const float* __restrict__ shared_y,
                                const float* __restrict__ shared_gate, void* out, int out_bf16,
-                               int add_to_out) {
+                               int add_to_out, int e_begin, int e_end) {
   const int t = blockIdx.x;
   int ord[16];
   int exp_id[16];
@@ -314,6 +319,8 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     for (int jj = 0; jj < k; ++jj) {
       const int j = ord[jj];
+      // Expert-parallel partial sums keep only this rank's experts.
+      if (exp_id[j] < e_begin || exp_id[j] >= e_end) continue;
       const int pos = inv_pos[(uint64_t)t * k + j];
       const float w = topk_w[(uint64_t)t * k + j];
       const float4 y = *reinterpret_cast<const float4*>(y_perm + (uint64_t)pos * H + h);
@@ -358,12 +365,13 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
 cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* topk_idx,
                            const float* topk_w, int T, int k, int H, const float* shared_y,
                            const float* shared_gate, void* out, bool out_bf16, bool add_to_out,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, int e_begin, int e_end) {
   if (T == 0) return cudaSuccess;
   const int threads = H >= 1024 ? 256 : 128;
   const dim3 grid(T, (H + threads * 4 - 1) / (threads * 4));
   combine_kernel<<<grid, threads, 0, stream>>>(y_perm, inv_pos, topk_idx, topk_w, k, H, shared_y,
-                                            shared_gate, out, out_bf16 ? 1 : 0, add_to_out ? 1 : 0);
+                                            shared_gate, out, out_bf16 ? 1 : 0, add_to_out ? 1 : 0,
+                                            e_begin, e_end);
   return cudaGetLastError();
 }
 
