@@ -249,6 +249,12 @@ def expert_bytes(T, U):
     return U * BYTES_PER_EXPERT + P * H * 2 + 2 * P * I * 2 + P * H * 4
 
 
+# DRAM bytes of one step's two expert-GEMM launches (read + written), from
+# one ncu capture of the 64-token workload: 604.9 + 6.8 MB (gate_up) and
+# 317.4 + 6.4 MB (down), against 891.3 MB algorithmic.
+TRAFFIC_T64 = 935.5e6
+
+
 def expert_flops(T):
     return 2.0 * T * TOP_K * 3 * H * I
 
@@ -341,7 +347,10 @@ def run_ours(args, rank, world, local):
     bytes_step = expert_bytes(args.tokens, U)
     achieved = bytes_step / (kern_ms / 1000.0) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                "frac": round(achieved / hbm_peak, 4),
+                "traffic": TRAFFIC_T64 if args.tokens == 64 else None,
+                "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of the gate_up and down "
+                                  "launches, one ncu capture of this 64-token workload" if args.tokens == 64 else None,
                 "kernel": "expert_gemm_kernel<NF4> (gate_up + down launches of one step)",
                 "algorithmic_bytes_per_step": bytes_step, "distinct_experts": U,
                 "kernel_ms_per_step": round(kern_ms, 4),

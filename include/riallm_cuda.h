@@ -196,7 +196,7 @@ int32_t riallm_cuda_moe_route(riallm_ctx* ctx, const riallm_qtensor* gate,
  * Limits: bf16 x/out ([T,H], 16-byte aligned), routed experts only (no
  * shared expert), the same shape rules as riallm_cuda_moe_forward, and the
  * call's scratch layout must fit 24 MiB (for hidden 4096 / intermediate
- * 14336, up to 469 token-expert pairs, T*k); larger calls return
+ * 14336, up to 472 token-expert pairs, T*k); larger calls return
  * RIALLM_ERR_MEMORY without launching anything. The first call on each
  * device looks up the array's device address (and sets kernel attributes);
  * make that first call before any stream capture. Every call reuses the same
