@@ -407,6 +407,7 @@ def run_ours(args, rank, world, local):
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
         cpu = cpu_baseline(rb, torch, d, blk)
+    streaming = None if args.no_stream else stream_measure(rb, torch, d, blk)
 
     if rank == 0:
         line = {
@@ -419,7 +420,7 @@ def run_ours(args, rank, world, local):
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": f"{launches_per_step} kernels per step (router, gather, expert gate_up and down GEMMs, combine) replayed from one CUDA graph",
             "captured_launches": per_step_launches,
-            "clocks": clk.summary(), "sweep": sweep,
+            "clocks": clk.summary(), "sweep": sweep, "streaming": streaming,
         }
         print(json.dumps(line), flush=True)
     del g
@@ -517,6 +518,51 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     return 0
 
 
+def stream_measure(rb, torch, d, blk, n_layers=4, depth=2):
+    """Streaming mode (ModelOptions.prefetch_layers): the block's NF4 layer
+    packed once into pinned host memory and streamed through a ring of
+    `depth` device slots, n_layers layers per pass (the same layer bytes
+    n_layers times), one 64-token decode batch per layer. Reports the H2D
+    rate of the copies and how much of the copy time the compute hides."""
+    from riallm_b200.streaming import LayerStreamer, PackedLayer
+    packed = PackedLayer({k: v for k, v in d.items()})
+    layers = [packed] * n_layers
+    s = LayerStreamer(layers, depth=depth, device=blk.x.device.index or 0)
+    x = blk.x
+
+    def fn(i, t):
+        rb.apply_moe(t, x, TOP_K, E)
+    s.run(fn)  # warm-up pass
+    torch.cuda.synchronize()
+    b0 = s.stats()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    passes = 3
+    start.record()
+    for _ in range(passes):
+        s.run(fn)
+    end.record()
+    torch.cuda.synchronize()
+    wall = start.elapsed_time(end) / passes
+    b1 = s.stats()
+    copy_ms = (b1["copy_ms"] - b0["copy_ms"]) / passes
+    nbytes = (b1["bytes"] - b0["bytes"]) / passes
+    start.record()
+    for _ in range(passes * n_layers):
+        rb.apply_moe(d, x, TOP_K, E)
+    end.record()
+    torch.cuda.synchronize()
+    compute = start.elapsed_time(end) / passes
+    s.close()
+    packed.close()
+    return {"layers_per_pass": n_layers, "prefetch_buffer_size": depth, "layer_bytes": packed.nbytes,
+            "ms_per_pass": round(wall, 3), "h2d_gbs": round(nbytes / (copy_ms / 1000.0) / 1e9, 2),
+            "h2d_gbs_wall": round(nbytes / (wall / 1000.0) / 1e9, 2),
+            "compute_ms_per_pass": round(compute, 3),
+            "exposed_copy_ms_per_pass": round(max(wall - compute, 0.0), 3),
+            "tokens_per_s": round(x.shape[0] / (wall / 1000.0), 1),
+            "note": "pinned host -> HBM over PCIe on a copy stream; copies of layers i+1 overlap layer i's block"}
+
+
 def cpu_baseline(rb, torch, d, blk):
     """The oracle's fp32 CPU port on the same weights, timed on this host's
     cores on a bounded sample (one full decode batch, repeated)."""
@@ -554,6 +600,7 @@ def main():
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--no-stream", action="store_true", help="skip the layer-streaming measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -116,6 +116,35 @@ int32_t riallm_cuda_stream_synchronize(riallm_ctx* ctx, void* stream);
 int32_t riallm_cuda_memory_stats(riallm_ctx* ctx, uint64_t* free_bytes,
                                  uint64_t* total_bytes);
 
+/* ---------------------------------------------------- layer streaming */
+
+/* Stands in for the per-forward device moves of a streamed layer
+ * (load_layer_to_device, src/model.rs:1131-1201; move_tensors_to_device,
+ * src/memory.rs:113-125) and acts on ModelOptions::prefetch_layers /
+ * prefetch_buffer_size (src/config.rs:389-393), which riallm leaves unused.
+ * A streamer holds `depth` device slots of `slot_bytes` (a multiple of 256)
+ * and a copy stream. device_slots is a caller buffer of depth * slot_bytes
+ * bytes (256-byte aligned), or NULL to allocate one. */
+typedef struct riallm_streamer riallm_streamer;
+int32_t riallm_cuda_streamer_create(riallm_ctx* ctx, int32_t depth, uint64_t slot_bytes,
+                                    void* device_slots, riallm_streamer** out);
+int32_t riallm_cuda_streamer_destroy(riallm_streamer* s);
+/* Copies `bytes` of a layer's packed weights from host_src (pinned host
+ * memory, or the copy is not asynchronous) into slot layer % depth on the
+ * copy stream, after the compute that last used the slot released it.
+ * RIALLM_ERR_CONFIG if that slot still holds an unreleased layer (prefetch
+ * at most depth layers ahead); RIALLM_ERR_MEMORY if bytes > slot_bytes. */
+int32_t riallm_cuda_streamer_prefetch(riallm_streamer* s, int32_t layer, const void* host_src,
+                                      uint64_t bytes);
+/* Makes `stream` wait for the layer's copy and returns its device address. */
+int32_t riallm_cuda_streamer_acquire(riallm_streamer* s, int32_t layer, void* stream, void** dptr);
+/* Marks the end of the layer's use on `stream` (after its last kernel). */
+int32_t riallm_cuda_streamer_release(riallm_streamer* s, int32_t layer, void* stream);
+/* Totals so far: bytes copied, copies, and the copies' device time (ms).
+ * Waits for the copy stream. */
+int32_t riallm_cuda_streamer_stats(riallm_streamer* s, uint64_t* bytes, uint64_t* copies,
+                                   double* copy_ms);
+
 /* ------------------------------------------------------ quantization */
 
 /* Number of scale/zero blocks and packed data bytes for numel elements. */
