@@ -169,15 +169,28 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs
   const int E = a.E, H = a.H, k = a.k;
   float* lg = sm;
   float* pr = sm + E;
+  // The token's row, as float32, staged once for the 8 warps (one round of
+  // independent 16-byte loads instead of a load chain per expert).
+  float* xs = sm + ((2 * E + (kRouterThreads / 32) * (E + 1) + E + 1 + 3) & ~3);
   const int nchunk = H >> 3;
   const uint64_t xrow = (uint64_t)t * H;
+  for (int c = threadIdx.x; c < nchunk; c += kRouterThreads) {
+    float xv[8];
+    load_chunk8(a.x, a.x_bf16 != 0, xrow + 8ull * c, xv);
+    *reinterpret_cast<float4*>(xs + 8 * c) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+    *reinterpret_cast<float4*>(xs + 8 * c + 4) = make_float4(xv[4], xv[5], xv[6], xv[7]);
+  }
+  __syncthreads();
   for (int e = warp; e < E; e += kRouterThreads / 32) {
     float acc = 0.0f;
     const uint64_t grow = (uint64_t)e * H;
-#pragma unroll 4
+#pragma unroll 8
     for (int c = lane; c < nchunk; c += 32) {
       float xv[8], wv[8];
-      load_chunk8(a.x, a.x_bf16 != 0, xrow + 8ull * c, xv);
+      const float4 x0 = *reinterpret_cast<const float4*>(xs + 8 * c);
+      const float4 x1 = *reinterpret_cast<const float4*>(xs + 8 * c + 4);
+      xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
+      xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
       gate_chunk8<QT>(a, grow + 8ull * c, wv);
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc = __fmaf_rn(xv[i], wv[i], acc);
@@ -233,8 +246,22 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs
 
 cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stream) {
   if (a.T <= 0) return cudaSuccess;
-  const size_t smem = (size_t)2 * a.E * sizeof(float) +
-                      (size_t)((kRouterThreads / 32) * (a.E + 1) + a.E + 1) * sizeof(int);
+  // logits + probabilities, pair-sort histograms, then the staged x row
+  // (16-byte aligned: the first part is padded to a multiple of 4 words).
+  const size_t words = ((size_t)2 * a.E + (size_t)(kRouterThreads / 32) * (a.E + 1) + a.E + 1 + 3) & ~(size_t)3;
+  const size_t smem = (size_t)a.H * sizeof(float) + words * sizeof(float);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(router_kernel<RIALLM_COMPRESSION_NONE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(router_kernel<RIALLM_COMPRESSION_FOUR_BIT>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(router_kernel<RIALLM_COMPRESSION_EIGHT_BIT>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
   if (gate_qtype == RIALLM_COMPRESSION_FOUR_BIT)
     router_kernel<RIALLM_COMPRESSION_FOUR_BIT><<<a.T, kRouterThreads, smem, stream>>>(a);
   else if (gate_qtype == RIALLM_COMPRESSION_EIGHT_BIT)
