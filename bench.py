@@ -408,6 +408,7 @@ def run_ours(args, rank, world, local):
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
         cpu = cpu_baseline(rb, torch, d, blk)
     streaming = None if args.no_stream else stream_measure(rb, torch, d, blk)
+    decode = None if args.no_decode else decode_measure(rb, torch, device)
 
     if rank == 0:
         line = {
@@ -420,7 +421,7 @@ def run_ours(args, rank, world, local):
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": f"{launches_per_step} kernels per step (router, gather, expert gate_up and down GEMMs, combine) replayed from one CUDA graph",
             "captured_launches": per_step_launches,
-            "clocks": clk.summary(), "sweep": sweep, "streaming": streaming,
+            "clocks": clk.summary(), "sweep": sweep, "streaming": streaming, "decode": decode,
         }
         print(json.dumps(line), flush=True)
     del g
@@ -563,6 +564,67 @@ def stream_measure(rb, torch, d, blk, n_layers=4, depth=2):
             "note": "pinned host -> HBM over PCIe on a copy stream; copies of layers i+1 overlap layer i's block"}
 
 
+def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_tokens=128, seed=3):
+    """Mixtral-8x7B (32 layers, 32/8 heads, V=32000) NF4 greedy decoding,
+    weights resident in HBM: prefill a prompt of `prompt_len` ids, then
+    `new_tokens` decode steps replayed from one CUDA graph per batch size
+    (all layers, LM head and argmax on the device). Timed with CUDA events
+    on the decoding stream."""
+    from riallm_b200 import decoder as D
+    cfg = D.DecoderConfig.mixtral_8x7b()
+    hbm_peak = load_peaks()[0]
+    t0 = time.perf_counter()
+    qw = D.synthetic_model(cfg, seed=seed, device=str(device))
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    model = D.Decoder(cfg, qw, max_batch=max(batches), max_seq=prompt_len + new_tokens, device=device.index or 0)
+    del qw
+    attn_bytes = ((cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim * cfg.hidden + cfg.hidden * cfg.heads * cfg.head_dim) * 2
+    lm_bytes = cfg.vocab * cfg.hidden * 2
+    out = {"model": "mixtral-8x7b: 32 layers, synthetic weights (seed 3), experts NF4, attention/embedding bf16",
+           "prompt_tokens": prompt_len, "new_tokens": new_tokens, "build_s": round(build_s, 2), "runs": []}
+    g = torch.Generator().manual_seed(seed)
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+    for B in batches:
+        prompt = torch.randint(0, cfg.vocab, (B, prompt_len), generator=g).to(device)
+        model.generate(prompt[:, :8], 2)  # warm-up: scratch arena, cuBLAS, the decode graph for B
+        graph, ids, _, nxt = model._decode_graph(B)
+        model.reset()
+        p0, p1, d0, d1 = ev(), ev(), ev(), ev()
+        torch.cuda.synchronize()
+        p0.record()
+        tok = torch.argmax(model.forward(prompt), -1)
+        p1.record()
+        d0.record()
+        for _ in range(new_tokens):
+            model._advance(B, 1)
+            ids.copy_(tok.view(B, 1))
+            graph.replay()
+            tok = nxt.clone()
+        d1.record()
+        torch.cuda.synchronize()
+        dec_ms = d0.elapsed_time(d1)
+        ms_tok = dec_ms / new_tokens
+        U = min(cfg.experts, cfg.top_k * B)
+        kv_read = B * cfg.kv_heads * (prompt_len + new_tokens // 2) * cfg.head_dim * 2 * 2
+        step_bytes = cfg.layers * (U * BYTES_PER_EXPERT + attn_bytes + kv_read) + lm_bytes
+        gbs = step_bytes / (ms_tok / 1000.0) / 1e9
+        pms = p0.elapsed_time(p1)
+        out["runs"].append({
+            "batch": B, "decode_tok_s": round(B * new_tokens / (dec_ms / 1000.0), 1),
+            "ms_per_decode_step": round(ms_tok, 3), "prefill_ms": round(pms, 2),
+            "prefill_tok_s": round(B * prompt_len / (pms / 1000.0), 1),
+            "step_bytes": int(step_bytes), "achieved_gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 4),
+            "bytes_note": "per decode step: 32 x (U NF4 experts + bf16 attention weights + mean KV-cache read) "
+                          f"+ LM head; U = min(8, 2 x batch) = {U}" + (" (exact)" if B == 1 else " (an upper bound)")})
+    model.close()
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
 def cpu_baseline(rb, torch, d, blk):
     """The oracle's fp32 CPU port on the same weights, timed on this host's
     cores on a bounded sample (one full decode batch, repeated)."""
@@ -601,6 +663,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--no-stream", action="store_true", help="skip the layer-streaming measurement")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Mixtral-8x7B decode measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -201,7 +201,11 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
                                    int32_t e_begin, int32_t e_local, void* stream);
 
 /* Grows the context's scratch arena for blocks up to these sizes now, so
- * that later riallm_cuda_moe_forward calls allocate nothing. */
+ * that later riallm_cuda_moe_forward calls allocate nothing. From then on
+ * the arena stays where it is: a CUDA graph that captured a call keeps
+ * using its address, so a later call that would need a larger arena fails
+ * with RIALLM_ERR_CONFIG instead of freeing it. Only another reserve grows
+ * it (graphs captured before that must not be replayed). */
 int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I,
                                 int32_t E, int32_t k, int32_t act_dtype);
 
@@ -253,6 +257,44 @@ typedef enum riallm_phase {
   RIALLM_PHASE_COMBINE = 5,  /* weighted combine */
   RIALLM_NUM_PHASES = 6
 } riallm_phase;
+
+/* ---------------------------------------------------------- decoder layer
+ * The dense parts of a decoder layer around the MoE block, for end-to-end
+ * decoding with a device-resident bf16 KV cache. riallm runs these through
+ * candle on each forward (src/model.rs:456-468, 912-1071, 1317-1328).
+ * Activations are bf16 (RIALLM_DTYPE_BF16 layout), arithmetic float32.
+ * Positions are a device int32 array pos[B]: row b*T + t of a call holds the
+ * token at position pos[b] + t, so one decode step can be graph-replayed
+ * while pos advances on the device. */
+
+/* RMSNorm, src/model.rs:456-468: out = bf16(x * rsqrt(mean(x^2) + eps) * w)
+ * per row of x [rows, H]. With delta != NULL the residual add
+ * x = bf16(x + delta) is stored back to x first. w is float32 [H].
+ * H % 8 == 0; x, delta and out 16-byte aligned. */
+int32_t riallm_cuda_rmsnorm(riallm_ctx* ctx, void* x, const void* delta, const float* w,
+                            void* out, int32_t rows, int32_t H, float eps, void* stream);
+
+/* Rotary embedding, src/model.rs:1002-1071 (rotate-half, angle =
+ * float(position) * inv_freq[i], i < d/2), of the q and k heads of
+ * qkv [B*T, (nh + 2*nkv) * d] (q heads, k heads, v heads). Rotated q goes to
+ * q_out [B*T, nh*d]; rotated k and the v heads are written into the caches
+ * [B, nkv, S_max, d] at each row's position. Positions outside [0, S_max)
+ * write nothing to the caches. */
+int32_t riallm_cuda_rope_kv_append(riallm_ctx* ctx, const void* qkv, const int32_t* pos,
+                                   int32_t B, int32_t T, int32_t nh, int32_t nkv, int32_t d,
+                                   const float* inv_freq, void* q_out, void* k_cache,
+                                   void* v_cache, int32_t S_max, void* stream);
+
+/* Causal grouped-query attention over the cache, src/model.rs:912-1000 with
+ * the query heads h of KV head h / (nh/nkv) (repeat_heads,
+ * src/model.rs:1317-1328): row b*T + t attends cache positions
+ * [0, pos[b] + t] (clamped to S_max) with scores q.k / sqrt(d), a softmax
+ * and the weighted sum of v, all float32. q and out are [B*T, nh*d].
+ * d is 64 or 128; nh / nkv is 1, 2, 4 or 8. */
+int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cache,
+                              const void* v_cache, const int32_t* pos, int32_t B, int32_t T,
+                              int32_t nh, int32_t nkv, int32_t d, int32_t S_max, void* out,
+                              void* stream);
 
 int32_t riallm_cuda_profile_enable(riallm_ctx* ctx, int32_t enable);
 int32_t riallm_cuda_profile_read(riallm_ctx* ctx, float* ms_per_phase,

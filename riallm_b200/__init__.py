@@ -123,6 +123,10 @@ SIGNATURES = {
     "riallm_cuda_streamer_release": (_i32, [_vp, _i32, _vp]),
     "riallm_cuda_streamer_stats": (_i32, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64),
                                           ctypes.POINTER(ctypes.c_double)]),
+    "riallm_cuda_rmsnorm": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, ctypes.c_float, _vp]),
+    "riallm_cuda_rope_kv_append": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp,
+                                          _i32, _vp]),
+    "riallm_cuda_attention": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
 }
 
 PHASES = ("route", "gather", "gate_up", "down", "shared", "combine")
@@ -257,7 +261,8 @@ class Context:
         if self.ptr:
             lib().riallm_cuda_ctx_destroy(self.ptr)
             self.ptr = None
-            Context._by_device.pop(self.device, None)
+            if Context._by_device.get(self.device) is self:
+                del Context._by_device[self.device]
 
 
 def _stream_ptr(t: torch.Tensor):

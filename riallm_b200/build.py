@@ -19,7 +19,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libriallm_cuda.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["api.cu", "quant.cu", "route.cu", "expert_tc.cu", "noalloc.cu", "stream.cu"]
+SOURCES = ["api.cu", "quant.cu", "route.cu", "expert_tc.cu", "noalloc.cu", "stream.cu", "decoder.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 
 NVCC_FLAGS = [

@@ -66,8 +66,13 @@ int check_qtensor(riallm_ctx* ctx, const riallm_qtensor& t, uint64_t numel, cons
   return RIALLM_OK;
 }
 
-int ensure_arena(riallm_ctx* ctx, uint64_t bytes) {
+int ensure_arena(riallm_ctx* ctx, uint64_t bytes, bool explicit_reserve = false) {
   if (ctx->arena_bytes >= bytes) return RIALLM_OK;
+  if (ctx->arena_reserved && !explicit_reserve)
+    return set_err(ctx, RIALLM_ERR_CONFIG,
+                   "call needs a larger MoE scratch arena than riallm_cuda_moe_reserve set aside (" +
+                       std::to_string(bytes) + " > " + std::to_string(ctx->arena_bytes) +
+                       " bytes); reserve for the largest token count first");
   if (ctx->arena) {
     RL_CUDA(ctx, cudaFree(ctx->arena), "cudaFree(arena)");
     ctx->arena = nullptr;
@@ -367,7 +372,9 @@ int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I
   if (int s = check_shapes(ctx, T, H, I, E, k)) return s;
   if (int s = set_device(ctx)) return s;
   MoeLayout L = rl::moe_layout(T, H, I, E, k, act_dtype, 0, ctx->num_sms);
-  return ensure_arena(ctx, L.total);
+  if (int s = ensure_arena(ctx, L.total, true)) return s;
+  ctx->arena_reserved = true;
+  return RIALLM_OK;
 }
 
 static int route_into(riallm_ctx* ctx, const riallm_qtensor& gate, const void* x, int T, int H, int E,

@@ -1,0 +1,330 @@
+// decoder.cu -- the dense parts of a Mixtral-style decoder layer that sit
+// around the MoE block, kept on the device with a bf16 KV cache:
+//   * RMSNorm (src/model.rs:456-468) with an optional fused residual add;
+//   * rotate-half rotary embedding (inv_freq = theta^(-2i/d),
+//     src/model.rs:1002-1071) of q and k, with k and v appended to the cache;
+//   * causal grouped-query attention over the cache (src/model.rs:912-1000,
+//     the query heads of one KV head sharing it as repeat_heads does,
+//     src/model.rs:1317-1328).
+// All arithmetic is float32 with bf16 inputs and outputs. Positions come from
+// a device array (one entry per sequence), so a decode step can be replayed
+// from a CUDA graph.
+#include <cfloat>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace {
+
+__device__ __forceinline__ float bf2f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+constexpr int kNormThreads = 256;
+
+// One CTA per row; H % 8 == 0 and rows 16-byte aligned (8 bf16 per load).
+// With delta: x = bf16(x + delta) is stored back before the norm.
+__global__ void __launch_bounds__(kNormThreads)
+    rmsnorm_kernel(uint16_t* __restrict__ x, const uint16_t* __restrict__ delta,
+                   const float* __restrict__ w, uint16_t* __restrict__ out, int H, float eps) {
+  const size_t r = blockIdx.x;
+  uint4* xr = reinterpret_cast<uint4*>(x + r * H);
+  const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + r * H) : nullptr;
+  const int nv = H / 8;
+  float ss = 0.f;
+  for (int v = threadIdx.x; v < nv; v += kNormThreads) {
+    uint4 a = xr[v];
+    uint16_t* ah = reinterpret_cast<uint16_t*>(&a);
+    if (dr) {
+      uint4 b = dr[v];
+      const uint16_t* bh = reinterpret_cast<const uint16_t*>(&b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ah[j] = f2bf(__fadd_rn(bf2f(ah[j]), bf2f(bh[j])));
+      xr[v] = a;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = bf2f(ah[j]);
+      ss = fmaf(f, f, ss);
+    }
+  }
+  __shared__ float red[kNormThreads / 32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+  const float inv = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)H), eps));
+  uint4* orow = reinterpret_cast<uint4*>(out + r * H);
+  for (int v = threadIdx.x; v < nv; v += kNormThreads) {
+    uint4 a = xr[v];  // this thread's own stores above, if any
+    const uint16_t* ah = reinterpret_cast<const uint16_t*>(&a);
+    uint4 o;
+    uint16_t* oh = reinterpret_cast<uint16_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) oh[j] = f2bf(__fmul_rn(__fmul_rn(bf2f(ah[j]), inv), w[v * 8 + j]));
+    orow[v] = o;
+  }
+}
+
+// One CTA per token row of qkv [B*T, (nh + 2 nkv) * d] (q heads, then k, then
+// v). Row b*T + t sits at position pos[b] + t; positions outside [0, S_max)
+// write nothing to the cache (the attention kernel clamps the same way).
+__global__ void __launch_bounds__(128)
+    rope_append_kernel(const uint16_t* __restrict__ qkv, const int* __restrict__ pos, int T, int nh,
+                       int nkv, int d, const float* __restrict__ inv_freq,
+                       uint16_t* __restrict__ q_out, uint16_t* __restrict__ kc,
+                       uint16_t* __restrict__ vc, int S_max) {
+  const int row = blockIdx.x;
+  const int b = row / T, t = row - b * T;
+  const int p = pos[b] + t;
+  const bool in_cache = p >= 0 && p < S_max;
+  const int half = d >> 1;
+  const uint16_t* src = qkv + (size_t)row * (nh + 2 * nkv) * d;
+  for (int i = threadIdx.x; i < (nh + nkv) * half; i += blockDim.x) {
+    const int h = i / half, j = i - h * half;
+    float s, c;
+    sincosf(__fmul_rn((float)p, inv_freq[j]), &s, &c);
+    const float x1 = bf2f(src[h * d + j]), x2 = bf2f(src[h * d + j + half]);
+    const uint16_t o1 = f2bf(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
+    const uint16_t o2 = f2bf(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
+    if (h < nh) {
+      uint16_t* q = q_out + (size_t)row * nh * d + (size_t)h * d;
+      q[j] = o1;
+      q[j + half] = o2;
+    } else if (in_cache) {
+      uint16_t* k = kc + (((size_t)b * nkv + (h - nh)) * S_max + p) * d;
+      k[j] = o1;
+      k[j + half] = o2;
+    }
+  }
+  if (in_cache) {
+    const uint16_t* vs = src + (size_t)(nh + nkv) * d;
+    for (int i = threadIdx.x; i < nkv * d; i += blockDim.x) {
+      const int h = i / d, j = i - h * d;
+      vc[(((size_t)b * nkv + h) * S_max + p) * d + j] = vs[i];
+    }
+  }
+}
+
+constexpr int kKeyChunk = 256;
+
+// CTA (t, kv head, b), D threads (one per head dimension): the REP query
+// heads of KV head kh for token t of sequence b attend keys [0, pos[b]+t].
+// Keys are taken kKeyChunk at a time: scores (a thread per key), the chunk's
+// max and exp-sum per head, then the weighted values (a thread per
+// dimension), rescaling the running sums online.
+template <int D, int REP>
+__global__ void __launch_bounds__(D)
+    attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
+                     const uint16_t* __restrict__ vc, const int* __restrict__ pos, int T, int nh,
+                     int nkv, int S_max, float scale, uint16_t* __restrict__ out) {
+  constexpr int NW = D / 32;
+  const int t = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
+  const size_t row = (size_t)b * T + t;
+  int L = pos[b] + t + 1;
+  L = L < 0 ? 0 : (L > S_max ? S_max : L);
+  __shared__ float qs[REP][D];
+  __shared__ float ps[REP][kKeyChunk];
+  __shared__ float red[REP][NW];
+  __shared__ float bc[REP];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) qs[r][i] = bf2f(q[row * nh * D + (size_t)(kh * REP + r) * D + i]);
+  __syncthreads();
+  const size_t base = ((size_t)b * nkv + kh) * S_max * D;
+  const uint16_t* kb = kc + base;
+  const uint16_t* vb = vc + base;
+  float acc[REP], m[REP], l[REP];
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    acc[r] = 0.f;
+    m[r] = -FLT_MAX;
+    l[r] = 0.f;
+  }
+  for (int c0 = 0; c0 < L; c0 += kKeyChunk) {
+    const int n = min(kKeyChunk, L - c0);
+    float cmax[REP];
+#pragma unroll
+    for (int r = 0; r < REP; ++r) cmax[r] = -FLT_MAX;
+    for (int j = i; j < n; j += D) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)(c0 + j) * D);
+      float s[REP];
+#pragma unroll
+      for (int r = 0; r < REP; ++r) s[r] = 0.f;
+#pragma unroll 4
+      for (int v = 0; v < D / 8; ++v) {
+        uint4 kv = kr[v];
+        const uint16_t* kh16 = reinterpret_cast<const uint16_t*>(&kv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float kf = bf2f(kh16[e]);
+#pragma unroll
+          for (int r = 0; r < REP; ++r) s[r] = fmaf(qs[r][v * 8 + e], kf, s[r]);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        const float sc = __fmul_rn(s[r], scale);
+        ps[r][j] = sc;
+        cmax[r] = fmaxf(cmax[r], sc);
+      }
+    }
+    // chunk maxima
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      float v = cmax[r];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+      if (lane == 0) red[r][warp] = v;
+    }
+    __syncthreads();
+    float mn[REP], corr[REP];
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      float v = red[r][0];
+#pragma unroll
+      for (int w = 1; w < NW; ++w) v = fmaxf(v, red[r][w]);
+      mn[r] = fmaxf(m[r], v);
+      corr[r] = expf(m[r] - mn[r]);
+      m[r] = mn[r];
+    }
+    __syncthreads();  // red is reused below
+    float csum[REP];
+#pragma unroll
+    for (int r = 0; r < REP; ++r) csum[r] = 0.f;
+    for (int j = i; j < n; j += D) {
+#pragma unroll
+      for (int r = 0; r < REP; ++r) {
+        const float e = expf(ps[r][j] - mn[r]);
+        ps[r][j] = e;
+        csum[r] += e;
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      float v = csum[r];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) red[r][warp] = v;
+    }
+    __syncthreads();
+    if (i < REP) {
+      float v = 0.f;
+      for (int w = 0; w < NW; ++w) v += red[i][w];
+      bc[i] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      l[r] = fmaf(l[r], corr[r], bc[r]);
+      acc[r] *= corr[r];
+    }
+    const uint16_t* vcol = vb + (size_t)c0 * D + i;
+#pragma unroll 8
+    for (int j = 0; j < n; ++j) {
+      const float vv = bf2f(vcol[(size_t)j * D]);
+#pragma unroll
+      for (int r = 0; r < REP; ++r) acc[r] = fmaf(ps[r][j], vv, acc[r]);
+    }
+    __syncthreads();  // ps and red are rewritten by the next chunk
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r)
+    out[row * nh * D + (size_t)(kh * REP + r) * D + i] = f2bf(L > 0 ? __fdiv_rn(acc[r], l[r]) : 0.f);
+}
+
+template <int D>
+cudaError_t launch_attention_d(int rep, dim3 grid, const uint16_t* q, const uint16_t* kc,
+                               const uint16_t* vc, const int* pos, int T, int nh, int nkv,
+                               int S_max, float scale, uint16_t* out, cudaStream_t st) {
+  switch (rep) {
+    case 1: attention_kernel<D, 1><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, out); break;
+    case 2: attention_kernel<D, 2><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, out); break;
+    case 4: attention_kernel<D, 4><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, out); break;
+    case 8: attention_kernel<D, 8><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, out); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int fail(riallm_ctx* ctx, int code, const char* msg) {
+  ctx->last_error = msg;
+  return code;
+}
+
+int launch_status(riallm_ctx* ctx, cudaError_t e, const char* what) {
+  if (e == cudaSuccess) {
+    ctx->launches += 1;
+    return RIALLM_OK;
+  }
+  ctx->last_error = std::string(what) + ": " + cudaGetErrorString(e);
+  return RIALLM_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t riallm_cuda_rmsnorm(riallm_ctx* ctx, void* x, const void* delta, const float* w, void* out,
+                            int32_t rows, int32_t H, float eps, void* stream) {
+  if (!ctx || !x || !w || !out) return RIALLM_ERR_INVALID;
+  if (rows < 0 || H <= 0 || H % 8 != 0) return fail(ctx, RIALLM_ERR_CONFIG, "rmsnorm: need H % 8 == 0");
+  if (!al16(x) || !al16(out) || (delta && !al16(delta)))
+    return fail(ctx, RIALLM_ERR_INVALID, "rmsnorm: buffers must be 16-byte aligned");
+  if (rows == 0) return RIALLM_OK;
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
+  rmsnorm_kernel<<<rows, kNormThreads, 0, (cudaStream_t)stream>>>(
+      static_cast<uint16_t*>(x), static_cast<const uint16_t*>(delta), w, static_cast<uint16_t*>(out), H, eps);
+  return launch_status(ctx, cudaGetLastError(), "rmsnorm launch");
+}
+
+int32_t riallm_cuda_rope_kv_append(riallm_ctx* ctx, const void* qkv, const int32_t* pos, int32_t B,
+                                   int32_t T, int32_t nh, int32_t nkv, int32_t d,
+                                   const float* inv_freq, void* q_out, void* k_cache,
+                                   void* v_cache, int32_t S_max, void* stream) {
+  if (!ctx || !qkv || !pos || !inv_freq || !q_out || !k_cache || !v_cache) return RIALLM_ERR_INVALID;
+  if (B < 0 || T < 0 || nh <= 0 || nkv <= 0 || d <= 0 || (d & 1) || S_max <= 0)
+    return fail(ctx, RIALLM_ERR_CONFIG, "rope_kv_append: bad dimensions");
+  if ((int64_t)B * T == 0) return RIALLM_OK;
+  if ((int64_t)B * T > (1ll << 31) - 1) return fail(ctx, RIALLM_ERR_CONFIG, "rope_kv_append: too many rows");
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
+  rope_append_kernel<<<B * T, 128, 0, (cudaStream_t)stream>>>(
+      static_cast<const uint16_t*>(qkv), pos, T, nh, nkv, d, inv_freq, static_cast<uint16_t*>(q_out),
+      static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), S_max);
+  return launch_status(ctx, cudaGetLastError(), "rope_kv_append launch");
+}
+
+int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cache, const void* v_cache,
+                              const int32_t* pos, int32_t B, int32_t T, int32_t nh, int32_t nkv,
+                              int32_t d, int32_t S_max, void* out, void* stream) {
+  if (!ctx || !q || !k_cache || !v_cache || !pos || !out) return RIALLM_ERR_INVALID;
+  if (B < 0 || T < 0 || nh <= 0 || nkv <= 0 || S_max <= 0 || nh % nkv != 0)
+    return fail(ctx, RIALLM_ERR_CONFIG, "attention: bad dimensions (heads must be a multiple of kv heads)");
+  const int rep = nh / nkv;
+  if (d != 64 && d != 128) return fail(ctx, RIALLM_ERR_CONFIG, "attention: head_dim must be 64 or 128");
+  if (rep != 1 && rep != 2 && rep != 4 && rep != 8)
+    return fail(ctx, RIALLM_ERR_CONFIG, "attention: heads / kv heads must be 1, 2, 4 or 8");
+  if (!al16(k_cache)) return fail(ctx, RIALLM_ERR_INVALID, "attention: k cache must be 16-byte aligned");
+  if (B > 65535 || nkv > 65535) return fail(ctx, RIALLM_ERR_CONFIG, "attention: batch or kv heads too large");
+  if ((int64_t)B * T == 0) return RIALLM_OK;
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
+  const dim3 grid(T, nkv, B);
+  const float scale = (float)(1.0 / sqrt((double)d));
+  auto* qq = static_cast<const uint16_t*>(q);
+  auto* kk = static_cast<const uint16_t*>(k_cache);
+  auto* vv = static_cast<const uint16_t*>(v_cache);
+  auto* oo = static_cast<uint16_t*>(out);
+  cudaError_t e = d == 128 ? launch_attention_d<128>(rep, grid, qq, kk, vv, pos, T, nh, nkv, S_max, scale, oo,
+                                                     (cudaStream_t)stream)
+                           : launch_attention_d<64>(rep, grid, qq, kk, vv, pos, T, nh, nkv, S_max, scale, oo,
+                                                    (cudaStream_t)stream);
+  return launch_status(ctx, e, "attention launch");
+}
+
+}  // extern "C"

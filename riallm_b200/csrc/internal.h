@@ -19,6 +19,10 @@ struct riallm_ctx {
   // never shrunk, freed with the context.
   void* arena = nullptr;
   uint64_t arena_bytes = 0;
+  // Set by riallm_cuda_moe_reserve: from then on a call never moves the
+  // arena (a CUDA graph that captured a call keeps its address); a call that
+  // needs more fails instead.
+  bool arena_reserved = false;
   // Device status word written by kernels whose bounded waits expired.
   int* d_status = nullptr;
   // Kernel launches issued by this context.

@@ -30,23 +30,13 @@ def _oracle_weights(O, qw):
     return out, shapes
 
 
-def test_greedy_decode_matches_oracle(rb, oracle_lib):
+def _check_against_oracle(O, cfg, qw, prompt, toks, logits):
+    """Teacher-forces the oracle decoder with the GPU's tokens."""
     from oracle.decoder_ref import DecoderRef
-    from riallm_b200 import decoder as D
-    cfg = D.DecoderConfig()
-    qw = D.quantize_weights(D.synthetic_weights(cfg, seed=0))
-    model = D.TinyDecoder(cfg, qw)
-    g = torch.Generator().manual_seed(1)
-    prompt = torch.randint(0, cfg.vocab, (64,), generator=g)
-    new = 16
-    toks, logits = model.generate(prompt.cuda(), new, keep_logits=True)
-    logits = logits.cpu().numpy()
-    assert len(toks) == new and logits.shape == (new, cfg.vocab)
-
-    ow, shapes = _oracle_weights(oracle_lib, qw)
+    ow, shapes = _oracle_weights(O, qw)
     ref = DecoderRef(cfg, ow, shapes)
-    feed, pos, flips = prompt.numpy(), 0, 0
-    for s in range(new):
+    feed, pos, flips = prompt, 0, 0
+    for s in range(len(toks)):
         r = ref.forward(feed, pos, last_only=True)[0]
         pos += len(feed)
         e = rel_err(logits[s], r)
@@ -58,3 +48,41 @@ def test_greedy_decode_matches_oracle(rb, oracle_lib):
             assert gap < TOL, f"step {s}: token {toks[s]} vs oracle {want}, gap {gap}"
         feed = np.array([toks[s]])
     assert flips <= 2
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    from riallm_b200 import decoder as D
+    cfg = D.DecoderConfig()
+    return cfg, D.quantize_weights(D.synthetic_weights(cfg, seed=0))
+
+
+def test_greedy_decode_matches_oracle(rb, oracle_lib, tiny):
+    """64-token prompt (ids U[0, 32000), seed 1), 16 greedy tokens."""
+    from riallm_b200 import decoder as D
+    cfg, qw = tiny
+    model = D.Decoder(cfg, qw)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, cfg.vocab, (64,), generator=g)
+    new = 16
+    toks, logits = model.generate(prompt.cuda(), new, keep_logits=True)
+    logits = logits.cpu().numpy()
+    assert len(toks) == new and logits.shape == (new, cfg.vocab)
+    _check_against_oracle(oracle_lib, cfg, qw, prompt.numpy(), toks, logits)
+    # the eager path (no CUDA graph) gives the same tokens
+    assert model.generate(prompt.cuda(), new, use_graph=False) == toks
+
+
+def test_batched_decode_matches_oracle(rb, oracle_lib, tiny):
+    """Two sequences decoded together, each checked against the oracle."""
+    from riallm_b200 import decoder as D
+    cfg, qw = tiny
+    model = D.Decoder(cfg, qw, max_batch=2, max_seq=128)
+    g = torch.Generator().manual_seed(2)
+    prompts = torch.randint(0, cfg.vocab, (2, 24), generator=g)
+    toks, logits = model.generate(prompts.cuda(), 8, keep_logits=True)
+    assert toks.shape == (2, 8) and logits.shape == (2, 8, cfg.vocab)
+    for b in range(2):
+        _check_against_oracle(oracle_lib, cfg, qw, prompts[b].numpy(), toks[b].tolist(), logits[b].cpu().numpy())
+    with pytest.raises(rb.ConfigError, match="max_seq"):
+        model.generate(prompts.cuda(), 200)

@@ -136,6 +136,30 @@ def test_add_to_out_and_empty(rb, oracle_lib):
     assert empty.shape == (0, H)
 
 
+def test_reserved_arena_does_not_move(rb, oracle_lib):
+    """After riallm_cuda_moe_reserve a call that needs a larger arena fails
+    (a captured graph may still use the old one); another reserve grows it."""
+    O = oracle_lib
+    H, I, E, k = 256, 256, 4, 2
+    w, _ = O.synthetic_layer(H, I, E, 1, seed=5)
+    d = set_shapes(dev_tensors(rb, w), H, I, E)
+    ctx = rb.Context(0)
+    try:
+        ctx.reserve(4, H, I, E, k, torch.bfloat16)
+        small = to_dev_x(O.synthetic_x(4, H, seed=6), True)
+        big = to_dev_x(O.synthetic_x(300, H, seed=7), True)
+        rb.apply_moe(d, small, k, E, ctx=ctx)
+        with pytest.raises(rb.ConfigError, match="reserve"):
+            rb.apply_moe(d, big, k, E, ctx=ctx)
+        ctx.reserve(300, H, I, E, k, torch.bfloat16)
+        out = rb.apply_moe(d, big, k, E, ctx=ctx)
+        ref, *_ = O.moe_forward(w, O.synthetic_x(300, H, seed=7), 300, H, I, E, k)
+        assert rel_err(out.float().cpu().numpy(), ref) < 2e-2
+    finally:
+        torch.cuda.synchronize()
+        ctx.close()
+
+
 def test_missing_tensor_and_bad_config(rb, oracle_lib):
     O = oracle_lib
     w, _ = O.synthetic_layer(256, 256, 4, 1, seed=1)
