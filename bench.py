@@ -408,7 +408,8 @@ def run_ours(args, rank, world, local):
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
         cpu = cpu_baseline(rb, torch, d, blk)
     streaming = None if args.no_stream else stream_measure(rb, torch, d, blk)
-    decode = None if args.no_decode else decode_measure(rb, torch, device)
+    decode = None if args.no_decode else decode_measure(rb, torch, device, decode_batches(args),
+                                                        new_tokens=args.decode_new)
 
     if rank == 0:
         line = {
@@ -564,6 +565,10 @@ def stream_measure(rb, torch, d, blk, n_layers=4, depth=2):
             "note": "pinned host -> HBM over PCIe on a copy stream; copies of layers i+1 overlap layer i's block"}
 
 
+def decode_batches(args):
+    return tuple(int(v) for v in args.decode_batches.split(",") if v)
+
+
 def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_tokens=128, seed=3):
     """Mixtral-8x7B (32 layers, 32/8 heads, V=32000) NF4 greedy decoding,
     weights resident in HBM: prefill a prompt of `prompt_len` ids, then
@@ -664,12 +669,23 @@ def main():
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--no-stream", action="store_true", help="skip the layer-streaming measurement")
     ap.add_argument("--no-decode", action="store_true", help="skip the Mixtral-8x7B decode measurement")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="run only the Mixtral-8x7B decode measurement and print its JSON")
+    ap.add_argument("--decode-batches", default="1,32", help="batch sizes of the decode measurement")
+    ap.add_argument("--decode-new", type=int, default=128, help="decode steps per batch size")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     rank, world, local = dist_setup()
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.decode_only:
+        import torch
+        import riallm_b200 as rb
+        torch.cuda.set_device(local)
+        r = decode_measure(rb, torch, torch.device("cuda", local), decode_batches(args), new_tokens=args.decode_new)
+        print(json.dumps({"decode": r}), flush=True)
+        return 0
     return run_ours(args, rank, world, local)
 
 

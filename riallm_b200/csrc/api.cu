@@ -220,7 +220,11 @@ int32_t riallm_cuda_ctx_create(int32_t device, riallm_ctx** out) {
   }
   ctx->num_sms = prop.multiProcessorCount;
   if (cudaMalloc(&ctx->d_status, sizeof(int)) != cudaSuccess ||
-      cudaMemset(ctx->d_status, 0, sizeof(int)) != cudaSuccess) {
+      cudaMemset(ctx->d_status, 0, sizeof(int)) != cudaSuccess ||
+      cudaMalloc(&ctx->attn_ws, rl::attn_ws_bytes(ctx->num_sms)) != cudaSuccess ||
+      cudaMemset(ctx->attn_ws, 0, rl::kAttnCounterBytes) != cudaSuccess) {
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->attn_ws) cudaFree(ctx->attn_ws);
     delete ctx;
     return RIALLM_ERR_MEMORY;
   }
@@ -233,6 +237,7 @@ int32_t riallm_cuda_ctx_destroy(riallm_ctx* ctx) {
   cudaSetDevice(ctx->device);
   if (ctx->arena) cudaFree(ctx->arena);
   if (ctx->d_status) cudaFree(ctx->d_status);
+  if (ctx->attn_ws) cudaFree(ctx->attn_ws);
   for (auto& pe : ctx->pending) {
     cudaEventDestroy(pe.start);
     cudaEventDestroy(pe.stop);

@@ -70,24 +70,39 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
-// One CTA per token row of qkv [B*T, (nh + 2 nkv) * d] (q heads, then k, then
-// v). Row b*T + t sits at position pos[b] + t; positions outside [0, S_max)
-// write nothing to the cache (the attention kernel clamps the same way).
+// CTA (row, head group): row b*T + t of qkv [B*T, (nh + 2 nkv) * d] (q heads,
+// then k heads, then v heads) sits at position pos[b] + t. Head group g
+// covers heads [8g, 8g + 8): q and k heads are rotated (q to q_out, k into
+// the cache), v heads copied into the cache. Positions outside [0, S_max)
+// write nothing to the caches (the attention kernel clamps the same way).
+constexpr int kRopeHeads = 8;
 __global__ void __launch_bounds__(128)
     rope_append_kernel(const uint16_t* __restrict__ qkv, const int* __restrict__ pos, int T, int nh,
                        int nkv, int d, const float* __restrict__ inv_freq,
                        uint16_t* __restrict__ q_out, uint16_t* __restrict__ kc,
                        uint16_t* __restrict__ vc, int S_max) {
+  __shared__ float cs[rl::kAttnMaxD / 2], sn[rl::kAttnMaxD / 2];
   const int row = blockIdx.x;
   const int b = row / T, t = row - b * T;
   const int p = pos[b] + t;
   const bool in_cache = p >= 0 && p < S_max;
   const int half = d >> 1;
+  const int h0 = blockIdx.y * kRopeHeads;
+  const int h1 = min(h0 + kRopeHeads, nh + 2 * nkv);
   const uint16_t* src = qkv + (size_t)row * (nh + 2 * nkv) * d;
-  for (int i = threadIdx.x; i < (nh + nkv) * half; i += blockDim.x) {
-    const int h = i / half, j = i - h * half;
-    float s, c;
-    sincosf(__fmul_rn((float)p, inv_freq[j]), &s, &c);
+  if (h0 < nh + nkv) {
+    for (int j = threadIdx.x; j < half; j += blockDim.x) {
+      float s_, c_;
+      sincosf(__fmul_rn((float)p, inv_freq[j]), &s_, &c_);
+      cs[j] = c_;
+      sn[j] = s_;
+    }
+    __syncthreads();
+  }
+  const int hr = min(h1, nh + nkv);  // rotated heads of this group: [h0, hr)
+  for (int i = threadIdx.x; i < (hr - h0) * half; i += blockDim.x) {
+    const int h = h0 + i / half, j = i % half;
+    const float c = cs[j], s = sn[j];
     const float x1 = bf2f(src[h * d + j]), x2 = bf2f(src[h * d + j + half]);
     const uint16_t o1 = f2bf(__fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s)));
     const uint16_t o2 = f2bf(__fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s)));
@@ -101,37 +116,45 @@ __global__ void __launch_bounds__(128)
       k[j + half] = o2;
     }
   }
-  if (in_cache) {
-    const uint16_t* vs = src + (size_t)(nh + nkv) * d;
-    for (int i = threadIdx.x; i < nkv * d; i += blockDim.x) {
-      const int h = i / d, j = i - h * d;
-      vc[(((size_t)b * nkv + h) * S_max + p) * d + j] = vs[i];
+  const int v0 = max(h0, nh + nkv);  // copied v heads: [v0, h1)
+  if (in_cache && v0 < h1) {
+    for (int i = threadIdx.x; i < (h1 - v0) * d; i += blockDim.x) {
+      const int h = v0 + i / d, j = i % d;
+      vc[(((size_t)b * nkv + (h - nh - nkv)) * S_max + p) * d + j] = src[(size_t)h * d + j];
     }
   }
 }
 
 constexpr int kKeyChunk = 256;
 
-// CTA (t, kv head, b), D threads (one per head dimension): the REP query
-// heads of KV head kh for token t of sequence b attend keys [0, pos[b]+t].
-// Keys are taken kKeyChunk at a time: scores (a thread per key), the chunk's
-// max and exp-sum per head, then the weighted values (a thread per
-// dimension), rescaling the running sums online.
+// CTA (t * nsplit + split, kv head, b), D threads (one per head dimension):
+// the REP query heads of KV head kh for token t of sequence b attend keys
+// [0, L), L = pos[b] + t + 1; split s takes the s-th of nsplit equal
+// contiguous key ranges. Keys are taken kKeyChunk at a time: scores (a
+// thread per key), the chunk's max and exp-sum per head, then the weighted
+// values (a thread per dimension), rescaling the running sums online. With
+// nsplit > 1 each CTA stores its maxima, sums and accumulators in ws and the
+// group's last CTA (a counter per group) merges them in split order.
 template <int D, int REP>
 __global__ void __launch_bounds__(D)
     attention_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ kc,
                      const uint16_t* __restrict__ vc, const int* __restrict__ pos, int T, int nh,
-                     int nkv, int S_max, float scale, uint16_t* __restrict__ out) {
+                     int nkv, int S_max, float scale, int nsplit, float* __restrict__ ws,
+                     unsigned* __restrict__ counters, uint16_t* __restrict__ out) {
   constexpr int NW = D / 32;
-  const int t = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
+  const int split = blockIdx.x % nsplit, t = blockIdx.x / nsplit;
+  const int kh = blockIdx.y, b = blockIdx.z;
   const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
   const size_t row = (size_t)b * T + t;
   int L = pos[b] + t + 1;
   L = L < 0 ? 0 : (L > S_max ? S_max : L);
+  const int per = (L + nsplit - 1) / nsplit;
+  const int k0 = min(L, split * per), k1 = min(L, k0 + per);
   __shared__ float qs[REP][D];
   __shared__ float ps[REP][kKeyChunk];
   __shared__ float red[REP][NW];
   __shared__ float bc[REP];
+  __shared__ unsigned last;
 #pragma unroll
   for (int r = 0; r < REP; ++r) qs[r][i] = bf2f(q[row * nh * D + (size_t)(kh * REP + r) * D + i]);
   __syncthreads();
@@ -145,8 +168,8 @@ __global__ void __launch_bounds__(D)
     m[r] = -FLT_MAX;
     l[r] = 0.f;
   }
-  for (int c0 = 0; c0 < L; c0 += kKeyChunk) {
-    const int n = min(kKeyChunk, L - c0);
+  for (int c0 = k0; c0 < k1; c0 += kKeyChunk) {
+    const int n = min(kKeyChunk, k1 - c0);
     float cmax[REP];
 #pragma unroll
     for (int r = 0; r < REP; ++r) cmax[r] = -FLT_MAX;
@@ -173,7 +196,6 @@ __global__ void __launch_bounds__(D)
         cmax[r] = fmaxf(cmax[r], sc);
       }
     }
-    // chunk maxima
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
       float v = cmax[r];
@@ -232,21 +254,65 @@ __global__ void __launch_bounds__(D)
     }
     __syncthreads();  // ps and red are rewritten by the next chunk
   }
+  uint16_t* orow = out + row * nh * D + (size_t)kh * REP * D + i;
+  if (nsplit == 1) {
 #pragma unroll
-  for (int r = 0; r < REP; ++r)
-    out[row * nh * D + (size_t)(kh * REP + r) * D + i] = f2bf(L > 0 ? __fdiv_rn(acc[r], l[r]) : 0.f);
+    for (int r = 0; r < REP; ++r) orow[(size_t)r * D] = f2bf(L > 0 ? __fdiv_rn(acc[r], l[r]) : 0.f);
+    return;
+  }
+  // Partial of this split: [m x REP][l x REP][acc REP x D].
+  constexpr int kSlot = REP * (D + 2);
+  const size_t group = ((size_t)b * nkv + kh) * T + t;
+  float* slot = ws + (group * nsplit + split) * kSlot;
+  if (i == 0) {
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      slot[r] = m[r];
+      slot[REP + r] = l[r];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r) slot[2 * REP + r * D + i] = acc[r];
+  __threadfence();
+  __syncthreads();
+  if (i == 0) last = atomicAdd(counters + group, 1u) == (unsigned)(nsplit - 1);
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const float* g0 = ws + group * nsplit * kSlot;
+#pragma unroll
+  for (int r = 0; r < REP; ++r) {
+    float M = -FLT_MAX;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(g0 + s * kSlot + r));
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float w = expf(__ldcg(g0 + s * kSlot + r) - M);
+      den = fmaf(w, __ldcg(g0 + s * kSlot + REP + r), den);
+      num = fmaf(w, __ldcg(g0 + s * kSlot + 2 * REP + r * D + i), num);
+    }
+    orow[(size_t)r * D] = f2bf(L > 0 ? __fdiv_rn(num, den) : 0.f);
+  }
+  if (i == 0) counters[group] = 0u;  // ready for the next call
 }
 
 template <int D>
 cudaError_t launch_attention_d(int rep, dim3 grid, const uint16_t* q, const uint16_t* kc,
                                const uint16_t* vc, const int* pos, int T, int nh, int nkv,
-                               int S_max, float scale, uint16_t* out, cudaStream_t st) {
+                               int S_max, float scale, int nsplit, float* ws, unsigned* counters,
+                               uint16_t* out, cudaStream_t st) {
   switch (rep) {
-    case 1: attention_kernel<D, 1><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, out); break;
-    case 2: attention_kernel<D, 2><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, out); break;
-    case 4: attention_kernel<D, 4><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, out); break;
-    case 8: attention_kernel<D, 8><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, out); break;
-    default: return cudaErrorInvalidValue;
+#define RL_ATTN_CASE(R)                                                                            \
+  case R:                                                                                          \
+    attention_kernel<D, R><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, nsplit, ws, \
+                                               counters, out);                                     \
+    break;
+    RL_ATTN_CASE(1)
+    RL_ATTN_CASE(2)
+    RL_ATTN_CASE(4)
+    RL_ATTN_CASE(8)
+#undef RL_ATTN_CASE
+    default:
+      return cudaErrorInvalidValue;
   }
   return cudaGetLastError();
 }
@@ -289,12 +355,14 @@ int32_t riallm_cuda_rope_kv_append(riallm_ctx* ctx, const void* qkv, const int32
                                    const float* inv_freq, void* q_out, void* k_cache,
                                    void* v_cache, int32_t S_max, void* stream) {
   if (!ctx || !qkv || !pos || !inv_freq || !q_out || !k_cache || !v_cache) return RIALLM_ERR_INVALID;
-  if (B < 0 || T < 0 || nh <= 0 || nkv <= 0 || d <= 0 || (d & 1) || S_max <= 0)
-    return fail(ctx, RIALLM_ERR_CONFIG, "rope_kv_append: bad dimensions");
+  if (B < 0 || T < 0 || nh <= 0 || nkv <= 0 || d <= 0 || (d & 1) || d > rl::kAttnMaxD || S_max <= 0)
+    return fail(ctx, RIALLM_ERR_CONFIG, "rope_kv_append: bad dimensions (head_dim even, <= 128)");
+  if ((int64_t)nh + 2 * nkv > 65535 * kRopeHeads) return fail(ctx, RIALLM_ERR_CONFIG, "rope_kv_append: too many heads");
   if ((int64_t)B * T == 0) return RIALLM_OK;
   if ((int64_t)B * T > (1ll << 31) - 1) return fail(ctx, RIALLM_ERR_CONFIG, "rope_kv_append: too many rows");
   if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
-  rope_append_kernel<<<B * T, 128, 0, (cudaStream_t)stream>>>(
+  const dim3 grid(B * T, (nh + 2 * nkv + kRopeHeads - 1) / kRopeHeads);
+  rope_append_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(
       static_cast<const uint16_t*>(qkv), pos, T, nh, nkv, d, inv_freq, static_cast<uint16_t*>(q_out),
       static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), S_max);
   return launch_status(ctx, cudaGetLastError(), "rope_kv_append launch");
@@ -314,16 +382,29 @@ int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cach
   if (B > 65535 || nkv > 65535) return fail(ctx, RIALLM_ERR_CONFIG, "attention: batch or kv heads too large");
   if ((int64_t)B * T == 0) return RIALLM_OK;
   if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
-  const dim3 grid(T, nkv, B);
+  // Split each (sequence, kv head, token) group's keys over several CTAs when
+  // the groups alone would leave SMs idle (decode at small batch).
+  const int64_t groups = (int64_t)B * T * nkv;
+  int nsplit = 1;
+  if (groups < 2ll * ctx->num_sms) {
+    nsplit = (int)((2ll * ctx->num_sms + groups - 1) / groups);
+    nsplit = min(nsplit, (int)(4ll * ctx->num_sms / groups));
+    nsplit = min(nsplit, 32);
+    nsplit = max(1, min(nsplit, S_max / 16));
+  }
+  if ((int64_t)T * nsplit > 0x7fffffffll) return fail(ctx, RIALLM_ERR_CONFIG, "attention: too many tokens");
+  const dim3 grid(T * nsplit, nkv, B);
   const float scale = (float)(1.0 / sqrt((double)d));
   auto* qq = static_cast<const uint16_t*>(q);
   auto* kk = static_cast<const uint16_t*>(k_cache);
   auto* vv = static_cast<const uint16_t*>(v_cache);
   auto* oo = static_cast<uint16_t*>(out);
-  cudaError_t e = d == 128 ? launch_attention_d<128>(rep, grid, qq, kk, vv, pos, T, nh, nkv, S_max, scale, oo,
-                                                     (cudaStream_t)stream)
-                           : launch_attention_d<64>(rep, grid, qq, kk, vv, pos, T, nh, nkv, S_max, scale, oo,
-                                                    (cudaStream_t)stream);
+  auto* counters = static_cast<unsigned*>(ctx->attn_ws);
+  float* ws = reinterpret_cast<float*>(static_cast<char*>(ctx->attn_ws) + rl::kAttnCounterBytes);
+  cudaError_t e = d == 128 ? launch_attention_d<128>(rep, grid, qq, kk, vv, pos, T, nh, nkv, S_max, scale, nsplit,
+                                                     ws, counters, oo, (cudaStream_t)stream)
+                           : launch_attention_d<64>(rep, grid, qq, kk, vv, pos, T, nh, nkv, S_max, scale, nsplit,
+                                                    ws, counters, oo, (cudaStream_t)stream);
   return launch_status(ctx, e, "attention launch");
 }
 

@@ -25,6 +25,9 @@ struct riallm_ctx {
   bool arena_reserved = false;
   // Device status word written by kernels whose bounded waits expired.
   int* d_status = nullptr;
+  // Split-key attention workspace (rl::attn_ws_bytes), allocated with the
+  // context so that graph-captured attention calls never see it move.
+  void* attn_ws = nullptr;
   // Kernel launches issued by this context.
   uint64_t launches = 0;
   // Phase profiling: event pairs recorded per call, summed on read.
@@ -39,6 +42,18 @@ struct riallm_ctx {
 };
 
 namespace rl {
+
+// Split-key attention: when the (sequence, kv head, token) groups of a call
+// fill fewer than 2 CTAs per SM, each group's keys are split over several
+// CTAs (at most 4 per SM in total) whose partial softmax sums are merged by
+// the group's last CTA. The workspace holds one completion counter per group
+// (zero between calls) and the partials: per CTA, REP maxima, REP sums and
+// REP x D accumulators (REP <= 8, D <= 128).
+constexpr int kAttnMaxRep = 8, kAttnMaxD = 128;
+constexpr uint64_t kAttnCounterBytes = 4096;
+inline uint64_t attn_ws_bytes(int num_sms) {
+  return kAttnCounterBytes + (uint64_t)4 * num_sms * kAttnMaxRep * (kAttnMaxD + 2) * sizeof(float);
+}
 
 // Offsets of the MoE scratch buffers inside one arena (all 1 KiB aligned).
 // The first kSyncBytes of a layout hold counters that must read zero

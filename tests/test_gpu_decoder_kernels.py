@@ -54,12 +54,18 @@ def _ref_attention(q, kc, vc, pos, T, nh, nkv, d):
     return out
 
 
-@pytest.mark.parametrize("nh,nkv,d", [(8, 2, 128), (4, 4, 64), (16, 2, 64)])
-def test_rope_append_and_attention(rb, nh, nkv, d):
+# (B, T, positions): small groups split each group's keys over several CTAs;
+# B*T*nkv >= 2 * 148 takes the one-CTA-per-group path.
+SHAPES = [(3, 4, [0, 9, 600]), (2, 80, [0, 300])]
+
+
+@pytest.mark.parametrize("nh,nkv,d,shape", [(8, 2, 128, 0), (4, 4, 64, 0), (16, 2, 64, 0), (8, 2, 128, 1)])
+def test_rope_append_and_attention(rb, nh, nkv, d, shape):
     from riallm_b200 import Context, lib
     from riallm_b200.decoder import apply_rope, rope_tables, inv_freq
-    B, T, S = 3, 4, 700
-    pos = torch.tensor([0, 9, 600], dtype=torch.int32, device="cuda")  # crosses the 256-key chunks
+    B, T, p0 = SHAPES[shape]
+    S = 700
+    pos = torch.tensor(p0, dtype=torch.int32, device="cuda")  # crosses the 256-key chunks
     g = torch.Generator(device="cuda").manual_seed(nh * 100 + d)
     kc = _bf(torch.randn(B, nkv, S, d, device="cuda", generator=g))
     vc = _bf(torch.randn(B, nkv, S, d, device="cuda", generator=g))
