@@ -177,7 +177,8 @@ int32_t riallm_cuda_dequantize(riallm_ctx* ctx, const riallm_qtensor* t,
  * FOUR_BIT or EIGHT_BIT; gate/shared tensors may be any compression.
  * Shape limits: H % 256 == 0, I % 256 == 0, E <= 256, k <= 16, k <= E.
  * Scratch comes from the context's device arena, which grows with
- * cudaMalloc on demand (see riallm_cuda_moe_reserve). */
+ * cudaMalloc on demand (see riallm_cuda_moe_reserve). Calls of one context
+ * share that arena: issue them on one stream (or order them). */
 int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w,
                                 const void* x, void* out, int32_t T, int32_t H,
                                 int32_t I, int32_t E, int32_t k,
@@ -201,11 +202,10 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
                                    int32_t e_begin, int32_t e_local, void* stream);
 
 /* Grows the context's scratch arena for blocks up to these sizes now, so
- * that later riallm_cuda_moe_forward calls allocate nothing. From then on
- * the arena stays where it is: a CUDA graph that captured a call keeps
- * using its address, so a later call that would need a larger arena fails
- * with RIALLM_ERR_CONFIG instead of freeing it. Only another reserve grows
- * it (graphs captured before that must not be replayed). */
+ * that later riallm_cuda_moe_forward calls allocate nothing (and can be
+ * captured in a CUDA graph). An arena outgrown by a later, larger call is
+ * kept until the context is destroyed, so graphs that captured earlier calls
+ * stay valid. */
 int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I,
                                 int32_t E, int32_t k, int32_t act_dtype);
 

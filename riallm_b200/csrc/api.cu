@@ -66,15 +66,11 @@ int check_qtensor(riallm_ctx* ctx, const riallm_qtensor& t, uint64_t numel, cons
   return RIALLM_OK;
 }
 
-int ensure_arena(riallm_ctx* ctx, uint64_t bytes, bool explicit_reserve = false) {
+int ensure_arena(riallm_ctx* ctx, uint64_t bytes) {
   if (ctx->arena_bytes >= bytes) return RIALLM_OK;
-  if (ctx->arena_reserved && !explicit_reserve)
-    return set_err(ctx, RIALLM_ERR_CONFIG,
-                   "call needs a larger MoE scratch arena than riallm_cuda_moe_reserve set aside (" +
-                       std::to_string(bytes) + " > " + std::to_string(ctx->arena_bytes) +
-                       " bytes); reserve for the largest token count first");
   if (ctx->arena) {
-    RL_CUDA(ctx, cudaFree(ctx->arena), "cudaFree(arena)");
+    // Kept, not freed: graphs that captured earlier calls still point at it.
+    ctx->retired_arenas.push_back(ctx->arena);
     ctx->arena = nullptr;
     ctx->arena_bytes = 0;
   }
@@ -236,6 +232,7 @@ int32_t riallm_cuda_ctx_destroy(riallm_ctx* ctx) {
   if (!ctx) return RIALLM_ERR_INVALID;
   cudaSetDevice(ctx->device);
   if (ctx->arena) cudaFree(ctx->arena);
+  for (void* a : ctx->retired_arenas) cudaFree(a);
   if (ctx->d_status) cudaFree(ctx->d_status);
   if (ctx->attn_ws) cudaFree(ctx->attn_ws);
   for (auto& pe : ctx->pending) {
@@ -377,9 +374,7 @@ int32_t riallm_cuda_moe_reserve(riallm_ctx* ctx, int32_t T, int32_t H, int32_t I
   if (int s = check_shapes(ctx, T, H, I, E, k)) return s;
   if (int s = set_device(ctx)) return s;
   MoeLayout L = rl::moe_layout(T, H, I, E, k, act_dtype, 0, ctx->num_sms);
-  if (int s = ensure_arena(ctx, L.total, true)) return s;
-  ctx->arena_reserved = true;
-  return RIALLM_OK;
+  return ensure_arena(ctx, L.total);
 }
 
 static int route_into(riallm_ctx* ctx, const riallm_qtensor& gate, const void* x, int T, int H, int E,

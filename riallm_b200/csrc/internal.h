@@ -19,10 +19,10 @@ struct riallm_ctx {
   // never shrunk, freed with the context.
   void* arena = nullptr;
   uint64_t arena_bytes = 0;
-  // Set by riallm_cuda_moe_reserve: from then on a call never moves the
-  // arena (a CUDA graph that captured a call keeps its address); a call that
-  // needs more fails instead.
-  bool arena_reserved = false;
+  // Arenas outgrown by a larger call. They stay allocated until the context
+  // is destroyed: a CUDA graph that captured an earlier call still uses its
+  // arena's address when it is replayed.
+  std::vector<void*> retired_arenas;
   // Device status word written by kernels whose bounded waits expired.
   int* d_status = nullptr;
   // Split-key attention workspace (rl::attn_ws_bytes), allocated with the

@@ -136,25 +136,35 @@ def test_add_to_out_and_empty(rb, oracle_lib):
     assert empty.shape == (0, H)
 
 
-def test_reserved_arena_does_not_move(rb, oracle_lib):
-    """After riallm_cuda_moe_reserve a call that needs a larger arena fails
-    (a captured graph may still use the old one); another reserve grows it."""
+def test_graph_survives_arena_growth(rb, oracle_lib):
+    """A CUDA graph captured at a small token count still replays correctly
+    after a larger call has grown the context's scratch arena (the outgrown
+    arena is kept, not freed)."""
     O = oracle_lib
     H, I, E, k = 256, 256, 4, 2
     w, _ = O.synthetic_layer(H, I, E, 1, seed=5)
     d = set_shapes(dev_tensors(rb, w), H, I, E)
     ctx = rb.Context(0)
     try:
+        x_np = O.synthetic_x(4, H, seed=6)
+        small = to_dev_x(x_np, True)
+        out = torch.empty_like(small)
         ctx.reserve(4, H, I, E, k, torch.bfloat16)
-        small = to_dev_x(O.synthetic_x(4, H, seed=6), True)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            rb.apply_moe(d, small, k, E, out=out, ctx=ctx)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            rb.apply_moe(d, small, k, E, out=out, ctx=ctx)
         big = to_dev_x(O.synthetic_x(300, H, seed=7), True)
-        rb.apply_moe(d, small, k, E, ctx=ctx)
-        with pytest.raises(rb.ConfigError, match="reserve"):
-            rb.apply_moe(d, big, k, E, ctx=ctx)
-        ctx.reserve(300, H, I, E, k, torch.bfloat16)
-        out = rb.apply_moe(d, big, k, E, ctx=ctx)
-        ref, *_ = O.moe_forward(w, O.synthetic_x(300, H, seed=7), 300, H, I, E, k)
+        rb.apply_moe(d, big, k, E, ctx=ctx)  # grows the arena
+        out.zero_()
+        g.replay()
+        ref, *_ = O.moe_forward(w, x_np, 4, H, I, E, k)
         assert rel_err(out.float().cpu().numpy(), ref) < 2e-2
+        del g
     finally:
         torch.cuda.synchronize()
         ctx.close()
