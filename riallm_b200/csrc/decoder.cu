@@ -28,6 +28,8 @@ constexpr int kNormThreads = 256;
 __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_kernel(uint16_t* __restrict__ x, const uint16_t* __restrict__ delta,
                    const float* __restrict__ w, uint16_t* __restrict__ out, int H, float eps) {
+  rl::pdl_wait();
+  rl::pdl_launch_dependents();
   const size_t r = blockIdx.x;
   uint4* xr = reinterpret_cast<uint4*>(x + r * H);
   const uint4* dr = delta ? reinterpret_cast<const uint4*>(delta + r * H) : nullptr;
@@ -82,6 +84,8 @@ __global__ void __launch_bounds__(128)
                        uint16_t* __restrict__ q_out, uint16_t* __restrict__ kc,
                        uint16_t* __restrict__ vc, int S_max) {
   __shared__ float cs[rl::kAttnMaxD / 2], sn[rl::kAttnMaxD / 2];
+  rl::pdl_wait();
+  rl::pdl_launch_dependents();
   const int row = blockIdx.x;
   const int b = row / T, t = row - b * T;
   const int p = pos[b] + t;
@@ -142,6 +146,8 @@ __global__ void __launch_bounds__(D)
                      int nkv, int S_max, float scale, int nsplit, float* __restrict__ ws,
                      unsigned* __restrict__ counters, uint16_t* __restrict__ out) {
   constexpr int NW = D / 32;
+  rl::pdl_wait();
+  rl::pdl_launch_dependents();
   const int split = blockIdx.x % nsplit, t = blockIdx.x / nsplit;
   const int kh = blockIdx.y, b = blockIdx.z;
   const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
@@ -279,18 +285,35 @@ __global__ void __launch_bounds__(D)
   __syncthreads();
   if (!last) return;
   __threadfence();
+  // Merge: the splits' maxima and sums are staged in shared memory (ps is
+  // free now; nsplit <= 32), thread r < REP turns them into weights
+  // exp(m_s - M) and the denominator, then every thread sums its dimension
+  // over the splits in split order.
   const float* g0 = ws + group * nsplit * kSlot;
+  for (int x = i; x < REP * nsplit; x += D) {
+    const int r = x / nsplit, sp = x - r * nsplit;
+    ps[r][sp] = __ldcg(g0 + sp * kSlot + r);
+    ps[r][32 + sp] = __ldcg(g0 + sp * kSlot + REP + r);
+  }
+  __syncthreads();
+  if (i < REP) {
+    float M = -FLT_MAX;
+    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, ps[i][sp]);
+    float den = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float w = expf(ps[i][sp] - M);
+      ps[i][sp] = w;
+      den = fmaf(w, ps[i][32 + sp], den);
+    }
+    bc[i] = den;
+  }
+  __syncthreads();
 #pragma unroll
   for (int r = 0; r < REP; ++r) {
-    float M = -FLT_MAX;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(g0 + s * kSlot + r));
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float w = expf(__ldcg(g0 + s * kSlot + r) - M);
-      den = fmaf(w, __ldcg(g0 + s * kSlot + REP + r), den);
-      num = fmaf(w, __ldcg(g0 + s * kSlot + 2 * REP + r * D + i), num);
-    }
-    orow[(size_t)r * D] = f2bf(L > 0 ? __fdiv_rn(num, den) : 0.f);
+    float num = 0.f;
+#pragma unroll 8
+    for (int sp = 0; sp < nsplit; ++sp) num = fmaf(ps[r][sp], __ldcg(g0 + sp * kSlot + 2 * REP + r * D + i), num);
+    orow[(size_t)r * D] = f2bf(L > 0 ? __fdiv_rn(num, bc[r]) : 0.f);
   }
   if (i == 0) counters[group] = 0u;  // ready for the next call
 }
@@ -301,11 +324,10 @@ cudaError_t launch_attention_d(int rep, dim3 grid, const uint16_t* q, const uint
                                int S_max, float scale, int nsplit, float* ws, unsigned* counters,
                                uint16_t* out, cudaStream_t st) {
   switch (rep) {
-#define RL_ATTN_CASE(R)                                                                            \
-  case R:                                                                                          \
-    attention_kernel<D, R><<<grid, D, 0, st>>>(q, kc, vc, pos, T, nh, nkv, S_max, scale, nsplit, ws, \
-                                               counters, out);                                     \
-    break;
+#define RL_ATTN_CASE(R)                                                                       \
+  case R:                                                                                     \
+    return rl::launch_pdl(attention_kernel<D, R>, grid, dim3(D), 0, st, q, kc, vc, pos, T, nh, nkv, S_max, \
+                      scale, nsplit, ws, counters, out);
     RL_ATTN_CASE(1)
     RL_ATTN_CASE(2)
     RL_ATTN_CASE(4)
@@ -345,9 +367,10 @@ int32_t riallm_cuda_rmsnorm(riallm_ctx* ctx, void* x, const void* delta, const f
     return fail(ctx, RIALLM_ERR_INVALID, "rmsnorm: buffers must be 16-byte aligned");
   if (rows == 0) return RIALLM_OK;
   if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
-  rmsnorm_kernel<<<rows, kNormThreads, 0, (cudaStream_t)stream>>>(
-      static_cast<uint16_t*>(x), static_cast<const uint16_t*>(delta), w, static_cast<uint16_t*>(out), H, eps);
-  return launch_status(ctx, cudaGetLastError(), "rmsnorm launch");
+  cudaError_t e = rl::launch_pdl(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, (cudaStream_t)stream,
+                             static_cast<uint16_t*>(x), static_cast<const uint16_t*>(delta), w,
+                             static_cast<uint16_t*>(out), H, eps);
+  return launch_status(ctx, e, "rmsnorm launch");
 }
 
 int32_t riallm_cuda_rope_kv_append(riallm_ctx* ctx, const void* qkv, const int32_t* pos, int32_t B,
@@ -362,10 +385,11 @@ int32_t riallm_cuda_rope_kv_append(riallm_ctx* ctx, const void* qkv, const int32
   if ((int64_t)B * T > (1ll << 31) - 1) return fail(ctx, RIALLM_ERR_CONFIG, "rope_kv_append: too many rows");
   if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
   const dim3 grid(B * T, (nh + 2 * nkv + kRopeHeads - 1) / kRopeHeads);
-  rope_append_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(
-      static_cast<const uint16_t*>(qkv), pos, T, nh, nkv, d, inv_freq, static_cast<uint16_t*>(q_out),
-      static_cast<uint16_t*>(k_cache), static_cast<uint16_t*>(v_cache), S_max);
-  return launch_status(ctx, cudaGetLastError(), "rope_kv_append launch");
+  cudaError_t e = rl::launch_pdl(rope_append_kernel, grid, dim3(128), 0, (cudaStream_t)stream,
+                             static_cast<const uint16_t*>(qkv), pos, T, nh, nkv, d, inv_freq,
+                             static_cast<uint16_t*>(q_out), static_cast<uint16_t*>(k_cache),
+                             static_cast<uint16_t*>(v_cache), S_max);
+  return launch_status(ctx, e, "rope_kv_append launch");
 }
 
 int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cache, const void* v_cache,
@@ -390,7 +414,7 @@ int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cach
     nsplit = (int)((2ll * ctx->num_sms + groups - 1) / groups);
     nsplit = min(nsplit, (int)(4ll * ctx->num_sms / groups));
     nsplit = min(nsplit, 32);
-    nsplit = max(1, min(nsplit, S_max / 16));
+    nsplit = max(1, min(nsplit, S_max / 64));  // at least 64 keys per split at full length
   }
   if ((int64_t)T * nsplit > 0x7fffffffll) return fail(ctx, RIALLM_ERR_CONFIG, "attention: too many tokens");
   const dim3 grid(T * nsplit, nkv, B);

@@ -164,6 +164,8 @@ template <int QT>
 __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs a) {
   extern __shared__ float sm[];
   __shared__ int is_last;
+  pdl_wait();  // x comes from the previous kernel; every output is read by earlier ones
+  pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
   const int E = a.E, H = a.H, k = a.k;
@@ -263,11 +265,11 @@ cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stre
     if (e != cudaSuccess) return e;
   }
   if (gate_qtype == RIALLM_COMPRESSION_FOUR_BIT)
-    router_kernel<RIALLM_COMPRESSION_FOUR_BIT><<<a.T, kRouterThreads, smem, stream>>>(a);
+    return launch_pdl(router_kernel<RIALLM_COMPRESSION_FOUR_BIT>, dim3(a.T), dim3(kRouterThreads), smem, stream, a);
   else if (gate_qtype == RIALLM_COMPRESSION_EIGHT_BIT)
-    router_kernel<RIALLM_COMPRESSION_EIGHT_BIT><<<a.T, kRouterThreads, smem, stream>>>(a);
+    return launch_pdl(router_kernel<RIALLM_COMPRESSION_EIGHT_BIT>, dim3(a.T), dim3(kRouterThreads), smem, stream, a);
   else
-    router_kernel<RIALLM_COMPRESSION_NONE><<<a.T, kRouterThreads, smem, stream>>>(a);
+    return launch_pdl(router_kernel<RIALLM_COMPRESSION_NONE>, dim3(a.T), dim3(kRouterThreads), smem, stream, a);
   return cudaGetLastError();
 }
 
@@ -279,8 +281,10 @@ __global__ void __launch_bounds__(256) gather_kernel(const void* __restrict__ x,
                                                      void* __restrict__ x_perm, int pair_perm,
                                                      const int* __restrict__ row_begin,
                                                      const int* __restrict__ row_end) {
-  // The expert GEMM that follows reads only the routing counts (final
-  // before this kernel started) until it waits for x_perm, so it may start.
+  // The router's outputs are final once this returns; the expert GEMM that
+  // follows reads only the routing counts until it waits for x_perm, so it
+  // may start now.
+  pdl_wait();
   pdl_launch_dependents();
   const int row = blockIdx.x;
   // Expert-parallel calls gather only the rows of this rank's experts.
@@ -311,8 +315,9 @@ cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int 
   if (P == 0) return cudaSuccess;
   const int n16 = H * (x_bf16 ? 2 : 4) / 16;
   const dim3 grid(P, (n16 + 255) / 256);
-  gather_kernel<<<grid, 256, 0, stream>>>(x, x_bf16 ? 1 : 0, perm_pair, k, H, x_perm,
-                                          (pair_perm && x_bf16) ? 1 : 0, row_begin, row_end);
+  cudaError_t e = launch_pdl(gather_kernel, grid, dim3(256), 0, stream, x, x_bf16 ? 1 : 0, perm_pair, k, H,
+                             x_perm, (pair_perm && x_bf16) ? 1 : 0, row_begin, row_end);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -324,6 +329,8 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
                                int k, int H, const float* __restrict__ shared_y,
                                const float* __restrict__ shared_gate, void* out, int out_bf16,
                                int add_to_out, int e_begin, int e_end) {
+  pdl_wait();  // y_perm comes from the down GEMM
+  pdl_launch_dependents();
   const int t = blockIdx.x;
   int ord[16];
   int exp_id[16];
@@ -396,10 +403,8 @@ cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* t
   if (T == 0) return cudaSuccess;
   const int threads = H >= 1024 ? 256 : 128;
   const dim3 grid(T, (H + threads * 4 - 1) / (threads * 4));
-  combine_kernel<<<grid, threads, 0, stream>>>(y_perm, inv_pos, topk_idx, topk_w, k, H, shared_y,
-                                            shared_gate, out, out_bf16 ? 1 : 0, add_to_out ? 1 : 0,
-                                            e_begin, e_end);
-  return cudaGetLastError();
+  return launch_pdl(combine_kernel, grid, dim3(threads), 0, stream, y_perm, inv_pos, topk_idx, topk_w, k, H,
+                    shared_y, shared_gate, out, out_bf16 ? 1 : 0, add_to_out ? 1 : 0, e_begin, e_end);
 }
 
 // ------------------------------------------------- CUDA-core grouped GEMM
