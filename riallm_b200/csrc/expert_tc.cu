@@ -78,6 +78,7 @@ constexpr int kRawOpBytes = 128 * 128;           // one operand: 128 rows x 128 
 constexpr int kRawPrmBytes = 128 * 16;           // one operand's 4 scales (or zeros) per row
 constexpr int kRawStageBytes = 2 * kRawOpBytes + 4 * kRawPrmBytes;  // 40 KiB
 constexpr int kMmaWarps = 4;
+constexpr int kMergeBuf = 64 * 1024;             // split-tile merge staging buffer (2, in the rings)
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarps = 4;
 constexpr int kWarpProd = 0, kWarpBProd = 1, kWarpMma0 = 2, kWarpDq0 = kWarpMma0 + kMmaWarps,
@@ -94,7 +95,7 @@ constexpr int kSmemPrm = (kRawStages * kRawStageBytes + kNarrowBBytes) > ((kRawS
                              ? kRawStages * kRawStageBytes + kNarrowBBytes
                              : (kRawStages - 1) * kRawStageBytes + kBRegionBytes;
 constexpr int kSmemBar = kSmemPrm + kParamSlots * 256 * 2 * 4;
-constexpr int kNumBars = 2 * kRawStages + 2 * kAStages + 2 + kMmaWarps;
+constexpr int kNumBars = 2 * kRawStages + 2 * kAStages + 2 + kMmaWarps + 4;
 constexpr int kSmemMisc = kSmemBar + 8 * 40;
 constexpr int kSmemTab = kSmemMisc + 16;
 constexpr int kSmemBytes = kSmemTab + 4 * (4 * kMaxE + 1) + 1024;  // + alignment slack
@@ -169,6 +170,25 @@ struct Sched {
     const uint64_t W = (uint64_t)(total - sk_tile0) * n_raw;
     w = W * blockIdx.x / G;
     w1 = W * (blockIdx.x + 1) / G;
+  }
+};
+
+// The CTAs after an owner whose stream-K shares start inside the owner's
+// tile (tile_end, in stream-K units), in CTA (= K) order; CTAs with empty
+// shares are skipped. next() returns gridDim.x when there are no more.
+struct ContribIter {
+  uint64_t b2;
+  __device__ __forceinline__ uint64_t next(uint64_t W, uint64_t G, uint64_t tile_end) {
+    while (b2 < G) {
+      const uint64_t c = b2++;
+      const uint64_t s0 = W * c / G;
+      if (s0 >= tile_end) {
+        b2 = G;
+        return G;
+      }
+      if (W * (c + 1) / G != s0) return c;
+    }
+    return G;
   }
 };
 
@@ -393,6 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* d_full = empty + kAStages;
   uint64_t* d_empty = d_full + 1;
   uint64_t* drain_bar = d_empty + 1;         // one per MMA issuer
+  uint64_t* mg_full = drain_bar + kMmaWarps; // split-tile merge: staging buffer b landed
+  uint64_t* mg_empty = mg_full + 2;          // staging buffer b read by the four epilogue warps
   uint32_t* tmem_base_s = reinterpret_cast<uint32_t*>(smem + kSmemMisc);
   volatile int* abort_s = reinterpret_cast<volatile int*>(smem + kSmemMisc + 4);
   int* max_nv_s = reinterpret_cast<int*>(smem + kSmemMisc + 8);
@@ -420,6 +442,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(d_full, n_iss);
     mbar_init(d_empty, kEpiWarps);
     for (int i = 0; i < kMmaWarps; ++i) mbar_init(&drain_bar[i], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&mg_full[b], 1);
+      mbar_init(&mg_empty[b], kEpiWarps);
+    }
     fence_mbar_init();
     *abort_s = 0;
   }
@@ -764,6 +790,61 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float* my_slot = part ? p.sk_ws + (uint64_t)blockIdx.x * slot_floats : nullptr;
       const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+      if (owner) {
+        // Add the later K ranges' partial sums into this CTA's (K half 0)
+        // accumulators in TMEM, in CTA (= K) order: deterministic. This is
+        // the CTA's last item, so its raw and token rings are idle: each
+        // partial operand ([column][row] f32, N columns) is bulk-copied into
+        // one of two staging buffers there while the other is being added.
+        const uint32_t part_bytes = (uint32_t)ti.N * 128u * 4u;
+        const bool issuer = warp == kWarpEpi0 && lane == 0;
+        ContribIter ci{blockIdx.x + 1}, cc{blockIdx.x + 1};
+        uint64_t ib2 = ci.next(W, G, tile_end);
+        uint32_t jn = 0;  // next (contributor, operand) job to copy
+        auto issue_next = [&]() -> bool {
+          if (ib2 >= G) return true;
+          const uint32_t b = jn & 1;
+          if (jn >= 2 && !mbar_wait(&mg_empty[b], ((jn - 2) >> 1) & 1, abort_s, p.status)) return false;
+          mbar_arrive_expect_tx(&mg_full[b], part_bytes);
+          bulk_load_g2s(smem + b * kMergeBuf, p.sk_ws + ib2 * slot_floats + (uint64_t)(jn & 1) * p.d_cols * 128,
+                        part_bytes, &mg_full[b]);
+          if (jn & 1) ib2 = ci.next(W, G, tile_end);
+          ++jn;
+          return true;
+        };
+        bool iok = true;
+        if (issuer) {
+          fence_proxy_async_global();
+          fence_proxy_async_smem();
+          iok = issue_next() && issue_next();
+        }
+        uint64_t cb2 = cc.next(W, G, tile_end);
+        for (uint32_t j = 0; cb2 < G && ok; ++j) {
+          const uint32_t b = j & 1, op = j & 1;
+          if (!warp_wait(&mg_full[b], (j >> 1) & 1, abort_s, p.status)) {
+            ok = false;
+            break;
+          }
+          const float* sb = reinterpret_cast<const float*>(smem + b * kMergeBuf);
+          const uint32_t acc = lane_base + op * (narrow ? acc_cols : 128u);
+          for (int n0 = 0; n0 < ti.N; n0 += 8) {
+            uint32_t v[8];
+            tmem_ld_32x32b_x8(acc + n0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj)
+              v[jj] = __float_as_uint(__fadd_rn(__uint_as_float(v[jj]), sb[(n0 + jj) * 128 + m]));
+            tmem_st_32x32b_x8(acc + n0, v);
+          }
+          tmem_wait_st();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&mg_empty[b]);
+          if (issuer && iok) iok = issue_next();
+          if (op == 1) cb2 = cc.next(W, G, tile_end);
+        }
+        ok = ok && __shfl_sync(0xffffffffu, iok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+      }
       for (int n0 = 0; n0 < ti.N; n0 += 8) {
         uint32_t g[8], u[8];
         if (narrow) {
@@ -793,21 +874,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             my_slot[(uint64_t)(p.d_cols + n0 + jj) * 128 + m] = __uint_as_float(u[jj]);
           }
           continue;
-        }
-        if (owner) {
-          // Add the later K ranges in CTA (= K) order: deterministic.
-          for (uint64_t b2 = blockIdx.x + 1; b2 < G; ++b2) {
-            const uint64_t s0 = W * b2 / G;
-            if (s0 >= tile_end) break;
-            if (W * (b2 + 1) / G == s0) continue;
-            const float* ws = p.sk_ws + b2 * slot_floats;
-#pragma unroll
-            for (int jj = 0; jj < 8; ++jj) {
-              g[jj] = __float_as_uint(__fadd_rn(__uint_as_float(g[jj]), __ldcg(ws + (uint64_t)(n0 + jj) * 128 + m)));
-              u[jj] = __float_as_uint(
-                  __fadd_rn(__uint_as_float(u[jj]), __ldcg(ws + (uint64_t)(p.d_cols + n0 + jj) * 128 + m)));
-            }
-          }
         }
         if (p.swiglu) {
           // When the down projection decodes NF4, h is stored in its K order:
