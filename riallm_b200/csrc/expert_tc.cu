@@ -827,14 +827,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const float* sb = reinterpret_cast<const float*>(smem + b * kMergeBuf);
           const uint32_t acc = lane_base + op * (narrow ? acc_cols : 128u);
-          for (int n0 = 0; n0 < ti.N; n0 += 8) {
-            uint32_t v[8];
-            tmem_ld_32x32b_x8(acc + n0, v);
+          // 32 columns per TMEM round trip (N is a multiple of 16).
+          for (int n0 = 0; n0 < ti.N; n0 += 32) {
+            const bool two = n0 + 16 < ti.N;
+            uint32_t v[32];
+            tmem_ld_32x32b_x16(acc + n0, *reinterpret_cast<uint32_t(*)[16]>(v));
+            if (two) tmem_ld_32x32b_x16(acc + n0 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
             tmem_wait_ld();
 #pragma unroll
-            for (int jj = 0; jj < 8; ++jj)
+            for (int jj = 0; jj < 16; ++jj)
               v[jj] = __float_as_uint(__fadd_rn(__uint_as_float(v[jj]), sb[(n0 + jj) * 128 + m]));
-            tmem_st_32x32b_x8(acc + n0, v);
+            tmem_st_32x32b_x16(acc + n0, v);
+            if (two) {
+#pragma unroll
+              for (int jj = 16; jj < 32; ++jj)
+                v[jj] = __float_as_uint(__fadd_rn(__uint_as_float(v[jj]), sb[(n0 + jj) * 128 + m]));
+              tmem_st_32x32b_x16(acc + n0 + 16, v + 16);
+            }
           }
           tmem_wait_st();
           __syncwarp();
