@@ -10,10 +10,13 @@ tokens (default: a decode batch of 64). The weights are larger than the
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Prints ONE JSON line on rank 0. Multi-GPU (torchrun, one rank per GPU): each
-rank runs an independent replica of the block on its own batch (weak
-scaling, no collective on the data path); value is the total tokens of all
-ranks over the slowest rank's device time.
+Prints ONE JSON line on rank 0. Multi-GPU (torchrun, one rank per GPU):
+expert parallel -- rank r keeps experts [r E/N, (r+1) E/N), every step
+all-gathers the ranks' batches (NCCL), runs its experts for all tokens and
+reduce-scatters the partial sums (weak scaling: 64 tokens per GPU); value
+is the total tokens of all ranks over the slowest rank's device time.
+The single-GPU line also carries a Mixtral-8x7B decode measurement (32
+layers, batch 1 and 32; --decode-only runs it alone).
 
 --impl reference times the oracle's CPU port of riallm's MoE block
 (oracle/riallm_oracle.c, all host threads) on the same workload; the Rust
@@ -358,23 +361,64 @@ def run_ours(args, rank, world, local):
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src,
                 "step_frac": round(U * BYTES_PER_EXPERT / (ms_per_step / 1000.0) / 1e9 / hbm_peak, 4)}
 
-    # End to end through the C ABI with host buffers: H2D of x from pinned
-    # memory, the block, D2H of the output, every step.
+    # End to end through the C ABI with host buffers: every step copies its
+    # x from pinned host memory (H2D), runs the block and copies the output
+    # back (D2H). The copies run on a second stream, double-buffered, so
+    # step i's block overlaps step i+1's H2D and step i-1's D2H; the timed
+    # region spans all of them (the copy stream is joined before the end).
     L = rb.lib()
+    blks = [blk, Block(rb, torch, d, args.tokens, device)]
+    blks[1].x.copy_(blk.x)
     nbytes = blk.x.numel() * 2
     hx = torch.empty_like(blk.x, device="cpu").pin_memory()
     hx.copy_(blk.x.cpu())
-    hout = torch.empty_like(hx).pin_memory()
-    st = torch.cuda.current_stream().cuda_stream
+    houts = [torch.empty_like(hx).pin_memory() for _ in range(2)]
+    comp = torch.cuda.current_stream()
+    copy = torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        blk.ctx.check(L.riallm_cuda_memcpy_h2d_async(blk.ctx.ptr, blk.x.data_ptr(), hx.data_ptr(), nbytes, st))
-        blk(st)
-        blk.ctx.check(L.riallm_cuda_memcpy_d2h_async(blk.ctx.ptr, hout.data_ptr(), blk.out.data_ptr(), nbytes, st))
-    e2e_ms = timed(torch, e2e_step, args.steps, args.warmup, dist, world)
+    def e2e_run(n):
+        cs, ks = copy.cuda_stream, comp.cuda_stream
+        copy.wait_stream(comp)
+        blk.ctx.check(L.riallm_cuda_memcpy_h2d_async(blk.ctx.ptr, blks[0].x.data_ptr(), hx.data_ptr(), nbytes, cs))
+        ev_in[0].record(copy)
+        for i in range(n):
+            b, nb = i % 2, (i + 1) % 2
+            if i + 1 < n:
+                if i >= 1:
+                    copy.wait_event(ev_done[nb])  # step i-1 has read blks[nb].x
+                blk.ctx.check(L.riallm_cuda_memcpy_h2d_async(blk.ctx.ptr, blks[nb].x.data_ptr(), hx.data_ptr(),
+                                                             nbytes, cs))
+                ev_in[nb].record(copy)
+            comp.wait_event(ev_in[b])
+            if i >= 2:
+                comp.wait_event(ev_out[b])  # step i-2's output has been copied out
+            blks[b](ks)
+            ev_done[b].record(comp)
+            copy.wait_event(ev_done[b])
+            blk.ctx.check(L.riallm_cuda_memcpy_d2h_async(blk.ctx.ptr, houts[b].data_ptr(), blks[b].out.data_ptr(),
+                                                         nbytes, cs))
+            ev_out[b].record(copy)
+        comp.wait_stream(copy)
+
+    e2e_run(args.warmup)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    e2e_run(args.steps)
+    t1.record()
+    torch.cuda.synchronize()
+    e2e_ms = t0.elapsed_time(t1)
+    if not torch.equal(houts[(args.steps - 1) % 2], blks[(args.steps - 1) % 2].out.cpu()):
+        raise RuntimeError("end-to-end output differs from the device-resident run")
     e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
-           "ms_per_step": round(e2e_ms / args.steps, 4)}
+           "ms_per_step": round(e2e_ms / args.steps, 4),
+           "note": "C ABI calls with pinned host buffers; H2D and D2H on a copy stream, double-buffered"}
 
     # Sweep over the other token counts of the configuration (rank-local).
     sweep = []
@@ -488,20 +532,59 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src}
 
     # End to end: this rank's tokens from pinned host memory, the block, the
-    # output back to the host, every step.
+    # output back to the host, every step; the copies run on a second stream,
+    # double-buffered, overlapping the neighbouring steps' blocks.
     hx = torch.empty_like(x, device="cpu").pin_memory()
     hx.copy_(x.cpu())
-    hout = torch.empty_like(hx).pin_memory()
+    houts = [torch.empty_like(hx).pin_memory() for _ in range(2)]
+    xs = [x, torch.empty_like(x)]
+    outs = [None, None]
+    comp = torch.cuda.current_stream()
+    copy = torch.cuda.Stream()
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_done = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        x.copy_(hx, non_blocking=True)
-        step()
-        hout.copy_(out, non_blocking=True)
-    e2e_ms = timed(torch, e2e_step, args.steps, args.warmup, dist, world)
+    def e2e_run(n):
+        copy.wait_stream(comp)
+        with torch.cuda.stream(copy):
+            xs[0].copy_(hx, non_blocking=True)
+        ev_in[0].record(copy)
+        for i in range(n):
+            b, nb = i % 2, (i + 1) % 2
+            if i + 1 < n:
+                if i >= 1:
+                    copy.wait_event(ev_done[nb])
+                with torch.cuda.stream(copy):
+                    xs[nb].copy_(hx, non_blocking=True)
+                ev_in[nb].record(copy)
+            comp.wait_event(ev_in[b])
+            if i >= 2:
+                comp.wait_event(ev_out[b])
+            outs[b] = blk(xs[b])
+            ev_done[b].record(comp)
+            copy.wait_event(ev_done[b])
+            with torch.cuda.stream(copy):
+                houts[b].copy_(outs[b], non_blocking=True)
+            ev_out[b].record(copy)
+        comp.wait_stream(copy)
+
+    e2e_run(args.warmup)
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    e2e_run(args.steps)
+    t1.record()
+    torch.cuda.synchronize()
+    tt = torch.tensor([t0.elapsed_time(t1)], device="cuda")
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    e2e_ms = float(tt.item())
     nbytes = x.numel() * 2
     e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
-           "ms_per_step": round(e2e_ms / args.steps, 4)}
+           "ms_per_step": round(e2e_ms / args.steps, 4),
+           "note": "per rank: pinned H2D of its tokens and D2H of its output on a copy stream, double-buffered"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
