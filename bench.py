@@ -653,11 +653,11 @@ def decode_batches(args):
 
 
 def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_tokens=128, seed=3):
-    """Mixtral-8x7B (32 layers, 32/8 heads, V=32000) NF4 greedy decoding,
-    weights resident in HBM: prefill a prompt of `prompt_len` ids, then
-    `new_tokens` decode steps replayed from one CUDA graph per batch size
-    (all layers, LM head and argmax on the device). Timed with CUDA events
-    on the decoding stream."""
+    """Mixtral-8x7B (32 layers, 32/8 heads, V=32000) NF4 decoding, weights
+    resident in HBM: prefill a prompt of `prompt_len` ids, then `new_tokens`
+    decode steps replayed from one CUDA graph per batch size (all layers, LM
+    head and argmax on the device), fed a seeded random continuation. Timed
+    with CUDA events on the decoding stream."""
     from riallm_b200 import decoder as D
     cfg = D.DecoderConfig.mixtral_8x7b()
     hbm_peak = load_peaks()[0]
@@ -665,7 +665,7 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
     qw = D.synthetic_model(cfg, seed=seed, device=str(device))
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
-    model = D.Decoder(cfg, qw, max_batch=max(batches), max_seq=prompt_len + new_tokens, device=device.index or 0)
+    model = D.Decoder(cfg, qw, max_batch=max(batches), max_seq=prompt_len + new_tokens + 1, device=device.index or 0)
     del qw
     attn_bytes = ((cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim * cfg.hidden + cfg.hidden * cfg.heads * cfg.head_dim) * 2
     lm_bytes = cfg.vocab * cfg.hidden * 2
@@ -679,25 +679,33 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
         prompt = torch.randint(0, cfg.vocab, (B, prompt_len), generator=g).to(device)
         model.generate(prompt[:, :8], 2)  # warm-up: scratch arena, cuBLAS, the decode graph for B
         graph, ids, _, nxt = model._decode_graph(B)
+        # Each decode step is fed the next ids of a seeded random continuation
+        # (teacher forcing): greedy decoding of random weights collapses every
+        # sequence onto one token, which would route all of them to the same
+        # experts. The step itself (all layers, LM head, argmax) is unchanged.
+        cont = torch.randint(0, cfg.vocab, (new_tokens + 1, B, 1), generator=g).to(device)
         model.reset()
         p0, p1, d0, d1 = ev(), ev(), ev(), ev()
         torch.cuda.synchronize()
         p0.record()
-        tok = torch.argmax(model.forward(prompt), -1)
+        model.forward(prompt)
         p1.record()
         d0.record()
-        for _ in range(new_tokens):
+        for i in range(new_tokens):
             model._advance(B, 1)
-            ids.copy_(tok.view(B, 1))
+            ids.copy_(cont[i])
             graph.replay()
-            tok = nxt.clone()
         d1.record()
         torch.cuda.synchronize()
         dec_ms = d0.elapsed_time(d1)
         ms_tok = dec_ms / new_tokens
-        U = min(cfg.experts, cfg.top_k * B)
+        # Experts each layer's block actually routed to, from one more decode
+        # step run eagerly (after the timed region) with a router probe.
+        used = []
+        model._forward(cont[new_tokens], experts_used=used)
+        U = sum(used) / len(used)
         kv_read = B * cfg.kv_heads * (prompt_len + new_tokens // 2) * cfg.head_dim * 2 * 2
-        step_bytes = cfg.layers * (U * BYTES_PER_EXPERT + attn_bytes + kv_read) + lm_bytes
+        step_bytes = sum(u * BYTES_PER_EXPERT for u in used) + cfg.layers * (attn_bytes + kv_read) + lm_bytes
         gbs = step_bytes / (ms_tok / 1000.0) / 1e9
         pms = p0.elapsed_time(p1)
         out["runs"].append({
@@ -705,8 +713,9 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
             "ms_per_decode_step": round(ms_tok, 3), "prefill_ms": round(pms, 2),
             "prefill_tok_s": round(B * prompt_len / (pms / 1000.0), 1),
             "step_bytes": int(step_bytes), "achieved_gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 4),
-            "bytes_note": "per decode step: 32 x (U NF4 experts + bf16 attention weights + mean KV-cache read) "
-                          f"+ LM head; U = min(8, 2 x batch) = {U}" + (" (exact)" if B == 1 else " (an upper bound)")})
+            "experts_per_layer": round(U, 2),
+            "bytes_note": "per decode step: the NF4 experts each layer routed to (counted on one more step) + "
+                          "32 x (bf16 attention weights + mean KV-cache read) + LM head"})
     model.close()
     del model
     torch.cuda.empty_cache()

@@ -39,7 +39,7 @@ from typing import Dict
 
 import torch
 
-from . import (CompressionType, ConfigError, Context, QuantizedTensor, apply_moe, lib, quantize_tensor)
+from . import (CompressionType, ConfigError, Context, QuantizedTensor, apply_moe, lib, quantize_tensor, route)
 
 
 @dataclass
@@ -217,9 +217,12 @@ class Decoder:
                                                  w.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1],
                                                  self.cfg.eps, self._st()))
 
-    def _forward(self, ids: torch.Tensor) -> torch.Tensor:
+    def _forward(self, ids: torch.Tensor, experts_used: list = None) -> torch.Tensor:
         """ids [B, T] on the device -> last-position logits [B, V] float32.
-        Appends T positions to every sequence (pos += T on the device)."""
+        Appends T positions to every sequence (pos += T on the device).
+        With experts_used (a list), the number of distinct experts each
+        layer's MoE block routes to is appended to it (an extra router pass;
+        eager use only)."""
         c, B, T = self.cfg, ids.shape[0], ids.shape[1]
         moe_ctx = self.ctx_step if T == 1 else self.ctx
         nh, nkv, d = c.heads, c.kv_heads, c.head_dim
@@ -240,6 +243,9 @@ class Decoder:
                                                    att.data_ptr(), self._st()))
             o = att @ layer["wo"].t()
             self._norm(h, layer["post_norm"], n, delta=o)         # h += o; n = norm(h)
+            if experts_used is not None:
+                counts = route(layer["moe"]["mlp.gate.weight"], n, c.top_k, c.experts, ctx=moe_ctx)[2]
+                experts_used.append(int((counts > 0).sum().item()))
             apply_moe(layer["moe"], n, c.top_k, c.experts, out=h, add_to_out=True, ctx=moe_ctx)
         self.pos[:B].add_(T)
         last = h.view(B, T, -1)[:, -1].contiguous()
