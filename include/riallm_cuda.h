@@ -290,7 +290,10 @@ int32_t riallm_cuda_rope_kv_append(riallm_ctx* ctx, const void* qkv, const int32
  * src/model.rs:1317-1328): row b*T + t attends cache positions
  * [0, pos[b] + t] (clamped to S_max) with scores q.k / sqrt(d), a softmax
  * and the weighted sum of v, all float32. q and out are [B*T, nh*d].
- * d is 64 or 128; nh / nkv is 1, 2, 4 or 8. */
+ * d is 64 or 128; nh / nkv is 1, 2, 4 or 8. When the (sequence, kv head,
+ * token) groups are too few to fill the GPU, each group's keys are split
+ * over several CTAs that merge through a workspace owned by the context:
+ * calls of one context must not overlap (issue them on one stream). */
 int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cache,
                               const void* v_cache, const int32_t* pos, int32_t B, int32_t T,
                               int32_t nh, int32_t nkv, int32_t d, int32_t S_max, void* out,
