@@ -299,6 +299,13 @@ int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cach
                               int32_t nh, int32_t nkv, int32_t d, int32_t S_max, void* out,
                               void* stream);
 
+/* y = bf16(x · wᵀ) with float32 accumulation for decode-sized batches: x
+ * [M, K], w [N, K] (a projection weight, e.g. q/k/v, o or the LM head,
+ * src/model.rs:912-940), y [M, N], all bf16; M <= 8, K % 256 == 0, x and w
+ * 16-byte aligned. The weight is streamed once. */
+int32_t riallm_cuda_linear_bf16(riallm_ctx* ctx, const void* x, const void* w, void* y, int32_t M,
+                                int32_t N, int32_t K, void* stream);
+
 int32_t riallm_cuda_profile_enable(riallm_ctx* ctx, int32_t enable);
 int32_t riallm_cuda_profile_read(riallm_ctx* ctx, float* ms_per_phase,
                                  uint64_t* calls);

@@ -127,6 +127,7 @@ SIGNATURES = {
     "riallm_cuda_rope_kv_append": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _vp,
                                           _i32, _vp]),
     "riallm_cuda_attention": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "riallm_cuda_linear_bf16": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
 }
 
 PHASES = ("route", "gather", "gate_up", "down", "shared", "combine")

@@ -129,6 +129,48 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// Skinny bf16 linear layer y = x · wᵀ for decode batches (M <= 8 rows of
+// x): the weight [N, K] is streamed once. Each warp takes whole output
+// columns n (rows of w): lane l reads 16-byte pieces l, l + 32, ... of w[n]
+// and the same pieces of every x row (L1-resident after the first warp),
+// accumulates M float32 dot products and the warp reduces them in a fixed
+// butterfly. K % 256 == 0.
+template <int M>
+__global__ void __launch_bounds__(256)
+    linear_bf16_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                       uint16_t* __restrict__ y, int N, int K) {
+  rl::pdl_wait();
+  rl::pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  const int kv = K >> 3;  // 16-byte pieces per row
+  for (int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); n < N; n += warps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(w + (size_t)n * K);
+    float acc[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = 0.f;
+#pragma unroll 4
+    for (int v = lane; v < kv; v += 32) {
+      const uint4 wv = __ldcs(wr + v);  // streamed once: evict first
+      const uint16_t* wh = reinterpret_cast<const uint16_t*>(&wv);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const uint4 xv = __ldg(reinterpret_cast<const uint4*>(x + (size_t)m * K) + v);
+        const uint16_t* xh = reinterpret_cast<const uint16_t*>(&xv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[m] = fmaf(bf2f(xh[e]), bf2f(wh[e]), acc[m]);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float a = acc[m];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) y[(size_t)m * N + n] = f2bf(a);
+    }
+  }
+}
+
 constexpr int kKeyChunk = 256;
 
 // CTA (t * nsplit + split, kv head, b), D threads (one per head dimension):
@@ -430,6 +472,43 @@ int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cach
                            : launch_attention_d<64>(rep, grid, qq, kk, vv, pos, T, nh, nkv, S_max, scale, nsplit,
                                                     ws, counters, oo, (cudaStream_t)stream);
   return launch_status(ctx, e, "attention launch");
+}
+
+int32_t riallm_cuda_linear_bf16(riallm_ctx* ctx, const void* x, const void* w, void* y, int32_t M,
+                                int32_t N, int32_t K, void* stream) {
+  if (!ctx || !x || !w || !y) return RIALLM_ERR_INVALID;
+  if (M < 0 || N < 0 || K <= 0 || M > 8 || K % 256 != 0)
+    return fail(ctx, RIALLM_ERR_CONFIG, "linear_bf16: need M <= 8 and K % 256 == 0");
+  if (!al16(x) || !al16(w)) return fail(ctx, RIALLM_ERR_INVALID, "linear_bf16: x and w must be 16-byte aligned");
+  if (M == 0 || N == 0) return RIALLM_OK;
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
+  const int warps_needed = N;
+  int blocks = (warps_needed + 7) / 8;
+  const int cap = ctx->num_sms * 8;  // 8 CTAs of 8 warps per SM at most
+  if (blocks > cap) blocks = cap;
+  auto* xx = static_cast<const uint16_t*>(x);
+  auto* ww = static_cast<const uint16_t*>(w);
+  auto* yy = static_cast<uint16_t*>(y);
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e;
+  switch (M) {
+#define RL_LIN_CASE(R) \
+  case R:              \
+    e = rl::launch_pdl(linear_bf16_kernel<R>, dim3(blocks), dim3(256), 0, st, xx, ww, yy, N, K); \
+    break;
+    RL_LIN_CASE(1)
+    RL_LIN_CASE(2)
+    RL_LIN_CASE(3)
+    RL_LIN_CASE(4)
+    RL_LIN_CASE(5)
+    RL_LIN_CASE(6)
+    RL_LIN_CASE(7)
+    RL_LIN_CASE(8)
+#undef RL_LIN_CASE
+    default:
+      e = cudaErrorInvalidValue;
+  }
+  return launch_status(ctx, e, "linear_bf16 launch");
 }
 
 }  // extern "C"

@@ -12,8 +12,10 @@ Kernels: RMSNorm (with the residual add fused), RoPE + KV-cache append and
 the attention are this library's (riallm_cuda_rmsnorm,
 riallm_cuda_rope_kv_append, riallm_cuda_attention); the MoE block is
 riallm_cuda_moe_forward adding into the residual stream (bf16, rounded
-once); the q/k/v (one fused weight), o and LM-head projections are cuBLAS
-bf16 GEMMs with float32 accumulation. Positions live in a device array, so
+once); the q/k/v (one fused weight), o and LM-head projections are bf16
+with float32 accumulation: riallm_cuda_linear_bf16 (the weight streamed
+once) for decode batches of up to 8 rows, cuBLAS GEMMs for prefill and
+larger batches. Positions live in a device array, so
 one decode step (all layers, LM head and the greedy argmax) is captured
 once in a CUDA graph and replayed per token.
 
@@ -217,6 +219,17 @@ class Decoder:
                                                  w.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1],
                                                  self.cfg.eps, self._st()))
 
+    def _linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """x [M, K] · wᵀ (w [N, K]) in bf16: riallm_cuda_linear_bf16 (weight
+        streamed once) for decode-sized M <= 8, cuBLAS otherwise."""
+        M, K = x.shape
+        if M > 8 or K % 256:
+            return x @ w.t()
+        y = torch.empty(M, w.shape[0], dtype=torch.bfloat16, device=self.dev)
+        self.ctx.check(lib().riallm_cuda_linear_bf16(self.ctx.ptr, x.data_ptr(), w.data_ptr(), y.data_ptr(), M,
+                                                     w.shape[0], K, self._st()))
+        return y
+
     def _forward(self, ids: torch.Tensor, experts_used: list = None) -> torch.Tensor:
         """ids [B, T] on the device -> last-position logits [B, V] float32.
         Appends T positions to every sequence (pos += T on the device).
@@ -233,7 +246,7 @@ class Decoder:
         L = lib()
         for i, layer in enumerate(self.layers):
             self._norm(h, layer["in_norm"], n)
-            qkv = n @ layer["wqkv"].t()
+            qkv = self._linear(n, layer["wqkv"])
             kc, vc = self.k_cache[i], self.v_cache[i]
             self.ctx.check(L.riallm_cuda_rope_kv_append(self.ctx.ptr, qkv.data_ptr(), self.pos.data_ptr(), B, T,
                                                         nh, nkv, d, self.inv_freq.data_ptr(), q.data_ptr(),
@@ -241,7 +254,7 @@ class Decoder:
             self.ctx.check(L.riallm_cuda_attention(self.ctx.ptr, q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
                                                    self.pos.data_ptr(), B, T, nh, nkv, d, self.max_seq,
                                                    att.data_ptr(), self._st()))
-            o = att @ layer["wo"].t()
+            o = self._linear(att, layer["wo"])
             self._norm(h, layer["post_norm"], n, delta=o)         # h += o; n = norm(h)
             if experts_used is not None:
                 counts = route(layer["moe"]["mlp.gate.weight"], n, c.top_k, c.experts, ctx=moe_ctx)[2]
@@ -251,7 +264,7 @@ class Decoder:
         last = h.view(B, T, -1)[:, -1].contiguous()
         nl = torch.empty_like(last)
         self._norm(last, self.final_norm, nl)
-        return (nl @ self.lm_head.t()).float()
+        return self._linear(nl, self.lm_head).float()
 
     def _advance(self, B: int, T: int):
         if B > self.max_batch:

@@ -111,3 +111,30 @@ def test_argument_errors(rb):
     with pytest.raises(ConfigError, match="1, 2, 4 or 8"):  # 6 heads over 2 kv heads = 3
         ctx.check(lib().riallm_cuda_attention(ctx.ptr, q.data_ptr(), kc.data_ptr(), kc.data_ptr(), pos.data_ptr(),
                                               1, 2, 6, 2, 128, 8, q.data_ptr(), st))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (3, 1000, 1024), (8, 4096, 4096), (2, 32000, 256)])
+def test_linear_bf16(rb, M, N, K):
+    """Skinny bf16 linear layer against a float32 torch matmul of the same
+    bf16 inputs (outputs are bf16: 1e-2 of max |ref|)."""
+    from riallm_b200 import Context, lib
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    x = _bf(torch.randn(M, K, device="cuda", generator=g))
+    w = _bf(torch.randn(N, K, device="cuda", generator=g) * 0.02)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    ctx = Context.get(0)
+    ctx.check(lib().riallm_cuda_linear_bf16(ctx.ptr, x.data_ptr(), w.data_ptr(), y.data_ptr(), M, N, K,
+                                            torch.cuda.current_stream().cuda_stream))
+    ref = x.float() @ w.float().t()
+    assert rel_err(y.float().cpu().numpy(), ref.cpu().numpy()) < 1e-2
+
+
+def test_linear_bf16_errors(rb):
+    from riallm_b200 import ConfigError, Context, lib
+    ctx = Context.get(0)
+    x = torch.zeros(9, 256, dtype=torch.bfloat16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    with pytest.raises(ConfigError, match="M <= 8"):
+        ctx.check(lib().riallm_cuda_linear_bf16(ctx.ptr, x.data_ptr(), x.data_ptr(), x.data_ptr(), 9, 256, 256, st))
+    with pytest.raises(ConfigError, match="K % 256"):
+        ctx.check(lib().riallm_cuda_linear_bf16(ctx.ptr, x.data_ptr(), x.data_ptr(), x.data_ptr(), 1, 2, 200, st))
