@@ -677,7 +677,7 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
         return torch.cuda.Event(enable_timing=True)
     for B in batches:
         prompt = torch.randint(0, cfg.vocab, (B, prompt_len), generator=g).to(device)
-        model.generate(prompt[:, :8], 2)  # warm-up: scratch arena, cuBLAS, the decode graph for B
+        model.generate(prompt, 2)  # warm-up: prefill shapes (cuBLAS, scratch arena), the decode graph for B
         graph, ids, _, nxt = model._decode_graph(B)
         # Each decode step is fed the next ids of a seeded random continuation
         # (teacher forcing): greedy decoding of random weights collapses every
