@@ -678,7 +678,6 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
     for B in batches:
         prompt = torch.randint(0, cfg.vocab, (B, prompt_len), generator=g).to(device)
         model.generate(prompt, 2)  # warm-up: prefill shapes (cuBLAS, scratch arena), the decode graph for B
-        graph, ids, _, nxt = model._decode_graph(B)
         # Each decode step is fed the next ids of a seeded random continuation
         # (teacher forcing): greedy decoding of random weights collapses every
         # sequence onto one token, which would route all of them to the same
@@ -691,18 +690,14 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
         model.forward(prompt)
         p1.record()
         d0.record()
-        for i in range(new_tokens):
-            model._advance(B, 1)
-            ids.copy_(cont[i])
-            graph.replay()
+        model.decode_forced(cont[:new_tokens])
         d1.record()
         torch.cuda.synchronize()
         dec_ms = d0.elapsed_time(d1)
         ms_tok = dec_ms / new_tokens
         # Experts each layer's block actually routed to, from one more decode
         # step run eagerly (after the timed region) with a router probe.
-        used = []
-        model._forward(cont[new_tokens], experts_used=used)
+        used = model.experts_per_layer(cont[new_tokens])
         U = sum(used) / len(used)
         kv_read = B * cfg.kv_heads * (prompt_len + new_tokens // 2) * cfg.head_dim * 2 * 2
         step_bytes = sum(u * BYTES_PER_EXPERT for u in used) + cfg.layers * (attn_bytes + kv_read) + lm_bytes

@@ -341,6 +341,26 @@ class Decoder:
             return res, (lk[0] if one else lk)
         return res
 
+    def decode_forced(self, ids: torch.Tensor) -> None:
+        """Decode steps fed given ids (teacher forcing): ids [S, B, 1] on the
+        device, one graph replay per step after a prefill; the logits and
+        greedy ids of each step are computed and dropped. Measures the decode
+        step with a chosen continuation."""
+        S, B = ids.shape[0], ids.shape[1]
+        g, buf, _, _ = self._decode_graph(B)
+        for i in range(S):
+            self._advance(B, 1)
+            buf.copy_(ids[i])
+            g.replay()
+
+    def experts_per_layer(self, ids: torch.Tensor) -> list:
+        """One eager decode step of ids [B, 1] that also counts, per layer,
+        the distinct experts its MoE block routes to."""
+        used = []
+        self._advance(ids.shape[0], ids.shape[1])
+        self._forward(ids.to(self.dev), experts_used=used)
+        return used
+
     def close(self):
         self._graphs.clear()
         torch.cuda.synchronize(self.dev)

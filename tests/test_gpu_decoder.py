@@ -86,3 +86,31 @@ def test_batched_decode_matches_oracle(rb, oracle_lib, tiny):
         _check_against_oracle(oracle_lib, cfg, qw, prompts[b].numpy(), toks[b].tolist(), logits[b].cpu().numpy())
     with pytest.raises(rb.ConfigError, match="max_seq"):
         model.generate(prompts.cuda(), 200)
+
+
+def test_forced_decode_and_expert_count(rb, tiny):
+    """Teacher-forced decode steps (graph replays) advance the cache like
+    eager steps: the logits of a following eager step match those of a model
+    that decoded the same ids eagerly; the router probe reports, per layer,
+    between top_k and E distinct experts."""
+    from riallm_b200 import decoder as D
+    cfg, qw = tiny
+    g = torch.Generator().manual_seed(4)
+    prompt = torch.randint(0, cfg.vocab, (2, 12), generator=g).cuda()
+    forced = torch.randint(0, cfg.vocab, (5, 2, 1), generator=g).cuda()
+    a, b = D.Decoder(cfg, qw, max_batch=2, max_seq=64), D.Decoder(cfg, qw, max_batch=2, max_seq=64)
+    a.reset()
+    a.forward(prompt)
+    a.decode_forced(forced)
+    b.reset()
+    b.forward(prompt)
+    for i in range(5):
+        b.forward(forced[i])
+    assert a.length == b.length == 17
+    nxt = torch.randint(0, cfg.vocab, (2, 1), generator=g).cuda()
+    la, lb = a.forward(nxt), b.forward(nxt)
+    assert rel_err(la.cpu().numpy(), lb.cpu().numpy()) < 1e-2
+    used = a.experts_per_layer(nxt)
+    assert len(used) == cfg.layers and all(cfg.top_k <= u <= cfg.experts for u in used)
+    a.close()
+    b.close()
