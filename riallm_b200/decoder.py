@@ -220,7 +220,7 @@ class Decoder:
 
     def _linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """x [M, K] · wᵀ (w [N, K]) in bf16: riallm_cuda_linear_bf16 (weight
-        streamed once; 1.6-2x cuBLAS at one row, measured) for a single row,
+        streamed once; faster than cuBLAS at one row) for a single row,
         cuBLAS otherwise (faster from two rows on)."""
         M, K = x.shape
         if M > 1 or K % 256:
