@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-constexpr int kKeyChunk = 256;
+constexpr int kKeyChunk = 64;
 
 // CTA (t * nsplit + split, kv head, b), D threads (one per head dimension):
 // the REP query heads of KV head kh for token t of sequence b attend keys
@@ -200,6 +200,11 @@ __global__ void __launch_bounds__(D)
   const int k0 = min(L, split * per), k1 = min(L, k0 + per);
   __shared__ float qs[REP][D];
   __shared__ float ps[REP][kKeyChunk];
+  // The chunk's key and value rows, staged with cp.async; key rows keep
+  // their 16-byte pieces XOR-swizzled by the row so that a thread per key
+  // reads them without bank conflicts.
+  __shared__ __align__(16) uint16_t ks[kKeyChunk][D];
+  __shared__ __align__(16) uint16_t vs[kKeyChunk][D];
   __shared__ float red[REP][NW];
   __shared__ float bc[REP];
   __shared__ unsigned last;
@@ -221,14 +226,22 @@ __global__ void __launch_bounds__(D)
     float cmax[REP];
 #pragma unroll
     for (int r = 0; r < REP; ++r) cmax[r] = -FLT_MAX;
+    constexpr int kPieces = D / 8;  // 16-byte pieces per row
+    for (int idx = i; idx < n * kPieces; idx += D) {
+      const int j = idx / kPieces, v = idx - j * kPieces;
+      rl::cp_async_16(&ks[j][(v ^ (j & 7)) * 8], kb + (size_t)(c0 + j) * D + v * 8);
+      rl::cp_async_16(&vs[j][v * 8], vb + (size_t)(c0 + j) * D + v * 8);
+    }
+    rl::cp_async_commit();
+    rl::cp_async_wait<0>();
+    __syncthreads();
     for (int j = i; j < n; j += D) {
-      const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)(c0 + j) * D);
       float s[REP];
 #pragma unroll
       for (int r = 0; r < REP; ++r) s[r] = 0.f;
 #pragma unroll 4
       for (int v = 0; v < D / 8; ++v) {
-        uint4 kv = kr[v];
+        uint4 kv = *reinterpret_cast<const uint4*>(&ks[j][(v ^ (j & 7)) * 8]);
         const uint16_t* kh16 = reinterpret_cast<const uint16_t*>(&kv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -293,10 +306,9 @@ __global__ void __launch_bounds__(D)
       l[r] = fmaf(l[r], corr[r], bc[r]);
       acc[r] *= corr[r];
     }
-    const uint16_t* vcol = vb + (size_t)c0 * D + i;
 #pragma unroll 8
     for (int j = 0; j < n; ++j) {
-      const float vv = bf2f(vcol[(size_t)j * D]);
+      const float vv = bf2f(vs[j][i]);
 #pragma unroll
       for (int r = 0; r < REP; ++r) acc[r] = fmaf(ps[r][j], vv, acc[r]);
     }
@@ -444,7 +456,8 @@ int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cach
   if (d != 64 && d != 128) return fail(ctx, RIALLM_ERR_CONFIG, "attention: head_dim must be 64 or 128");
   if (rep != 1 && rep != 2 && rep != 4 && rep != 8)
     return fail(ctx, RIALLM_ERR_CONFIG, "attention: heads / kv heads must be 1, 2, 4 or 8");
-  if (!al16(k_cache)) return fail(ctx, RIALLM_ERR_INVALID, "attention: k cache must be 16-byte aligned");
+  if (!al16(k_cache) || !al16(v_cache))
+    return fail(ctx, RIALLM_ERR_INVALID, "attention: k and v caches must be 16-byte aligned");
   if (B > 65535 || nkv > 65535) return fail(ctx, RIALLM_ERR_CONFIG, "attention: batch or kv heads too large");
   if ((int64_t)B * T == 0) return RIALLM_OK;
   if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, RIALLM_ERR_CUDA, "cudaSetDevice");
