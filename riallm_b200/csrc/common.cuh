@@ -114,6 +114,12 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// Prefetches [p, p + bytes) of global memory into L2 (bulk, no data
+// returned); p and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Untiled bulk copy (no multicast) of `bytes` (a multiple of 16; both
 // addresses 16-byte aligned) from this GPU's global memory into this CTA's
 // shared memory, completing on `bar` with its byte count.

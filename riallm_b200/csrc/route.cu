@@ -156,6 +156,23 @@ __device__ void permute_block(const int* topk_idx, int P, int E, int* counts, in
   }
 }
 
+// Bulk L2 prefetch of this CTA's 1/gridDim share of [base, base + bytes),
+// trimmed to 16-byte boundaries inside the buffer.
+__device__ __forceinline__ void prefetch_share(const void* base, uint64_t bytes) {
+  if (!base || bytes == 0) return;
+  const uint64_t b = reinterpret_cast<uint64_t>(base), e = b + bytes;
+  const uint64_t per = (bytes + gridDim.x - 1) / gridDim.x;
+  uint64_t lo = b + per * blockIdx.x, hi = lo + per;
+  if (hi > e) hi = e;
+  lo = (lo + 15) & ~uint64_t(15);
+  hi &= ~uint64_t(15);
+  while (lo < hi) {
+    const uint64_t n = hi - lo < (1u << 20) ? hi - lo : (1u << 20);
+    bulk_prefetch_l2(reinterpret_cast<const void*>(lo), (uint32_t)n);
+    lo += n;
+  }
+}
+
 // One CTA per token: warp w computes the logits of experts w, w+8, ...
 // (decoding the router weight on the fly), warp 0 then takes the softmax
 // and the top k. The CTA that finishes last (a counter in device memory,
@@ -164,6 +181,18 @@ template <int QT>
 __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs a) {
   extern __shared__ float sm[];
   __shared__ int is_last;
+  // The router weight does not depend on the previous kernel: while it
+  // drains, pull this CTA's share of it into L2 (the loads below then hit L2).
+  if (threadIdx.x == 0) {
+    const uint64_t wbytes = QT == RIALLM_COMPRESSION_FOUR_BIT ? (uint64_t)a.E * a.H / 2
+                            : QT == RIALLM_COMPRESSION_EIGHT_BIT ? (uint64_t)a.E * a.H
+                                                                 : (uint64_t)a.E * a.H * 4;
+    prefetch_share(a.gdata, wbytes);
+    if (QT != RIALLM_COMPRESSION_NONE) {
+      prefetch_share(a.gscales, a.n_scales * 4);
+      prefetch_share(a.gzeros, a.n_zeros * 4);
+    }
+  }
   pdl_wait();  // x comes from the previous kernel; every output is read by earlier ones
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
