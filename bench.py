@@ -454,6 +454,7 @@ def run_ours(args, rank, world, local):
     streaming = None if args.no_stream else stream_measure(rb, torch, d, blk)
     decode = None if args.no_decode else decode_measure(rb, torch, device, decode_batches(args),
                                                         new_tokens=args.decode_new)
+    fine = None if args.no_sweep else fine_grained_measure(rb, torch, device)
 
     if rank == 0:
         line = {
@@ -466,7 +467,7 @@ def run_ours(args, rank, world, local):
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": f"{launches_per_step} kernels per step (router, gather, expert gate_up and down GEMMs, combine) replayed from one CUDA graph",
             "captured_launches": per_step_launches,
-            "clocks": clk.summary(), "sweep": sweep, "streaming": streaming, "decode": decode,
+            "clocks": clk.summary(), "sweep": sweep, "streaming": streaming, "decode": decode, "fine_grained": fine,
         }
         print(json.dumps(line), flush=True)
     del g
@@ -715,6 +716,59 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
     del model
     torch.cuda.empty_cache()
     return out
+
+
+def fine_grained_measure(rb, torch, device, steps=20):
+    """The fine-grained MoE configuration (hidden 2048, 128 experts, top-8,
+    intermediate 768; N(0, 0.02) weights, seed 4): a 64-token decode batch
+    with NF4 and with 8-bit experts, and an 8192-token prefill with NF4.
+    Expert-GEMM time from the library's phase events; one block call per
+    step."""
+    import ctypes as C
+    Hf, If, Ef, kf = 2048, 768, 128, 8
+    L = rb.lib()
+    ctx = rb.Context.get(device.index or 0)
+    hbm_peak, bf16_peak, _, _ = load_peaks()
+    out = {"config": "fine-grained: hidden 2048, 128 experts, top-8, intermediate 768", "runs": []}
+    for qt, T in ((rb.CompressionType.FourBit, 64), (rb.CompressionType.EightBit, 64),
+                  (rb.CompressionType.FourBit, 8192)):
+        g = torch.Generator(device=device).manual_seed(4)
+        d = {"mlp.gate.weight": rb.quantize_tensor(torch.randn(Ef, Hf, device=device, generator=g) * 0.02, qt),
+             "mlp.experts.gate_up_proj": rb.quantize_tensor(
+                 torch.randn(Ef, 2 * If, Hf, device=device, generator=g) * 0.02, qt),
+             "mlp.experts.down_proj": rb.quantize_tensor(torch.randn(Ef, Hf, If, device=device, generator=g) * 0.02, qt)}
+        x = torch.randn(T, Hf, device=device, generator=g).to(torch.bfloat16)
+        counts = rb.route(d["mlp.gate.weight"], x, kf, Ef)[2]
+        U = int((counts > 0).sum().item())
+        for _ in range(3):
+            rb.apply_moe(d, x, kf, Ef)
+        ms = timed(torch, lambda: rb.apply_moe(d, x, kf, Ef), steps, 3, None, 1)
+        ph, _ = phase_profile(torch, _Call(rb, d, x, kf, Ef, ctx), max(steps, 10))
+        kern_ms = ph["gate_up"] + ph["down"]
+        bpw = 0.625 if qt == rb.CompressionType.FourBit else 1.0 + 8.0 / 128.0
+        run = {"qtype": qt.name, "tokens": T, "tokens_per_s": round(T * steps / (ms / 1000.0), 1),
+               "ms_per_step": round(ms / steps, 4), "distinct_experts": U, "kernel_ms": round(kern_ms, 4)}
+        if T <= 512:
+            bytes_step = U * 3 * Hf * If * bpw
+            gbs = bytes_step / (kern_ms / 1000.0) / 1e9
+            run.update({"bound": "hbm", "achieved_gbs": round(gbs, 1), "frac": round(gbs / hbm_peak, 4)})
+        else:
+            tf = 2.0 * T * kf * 3 * Hf * If / (kern_ms / 1000.0) / 1e12
+            run.update({"bound": "tensor", "achieved_tflops": round(tf, 1), "frac_of_burst_peak": round(tf / bf16_peak, 4)})
+        out["runs"].append(run)
+        del d
+        torch.cuda.empty_cache()
+    return out
+
+
+class _Call:
+    """A block call in the shape phase_profile expects."""
+
+    def __init__(self, rb, d, x, k, E, ctx):
+        self.rb, self.d, self.x, self.k, self.E, self.ctx = rb, d, x, k, E, ctx
+
+    def __call__(self, stream_ptr=None):
+        self.rb.apply_moe(self.d, self.x, self.k, self.E)
 
 
 def cpu_baseline(rb, torch, d, blk):

@@ -297,7 +297,7 @@ def np_dequantize_int8(data, scales, zeros, block_size=128):
 # ------------------------------------------------------------- synthetic layers
 
 def synthetic_layer(H: int, I: int, E: int, qtype: int, seed: int, std: float = 0.02,
-                    shared_intermediate: int = 0, zipf_bias: bool = False):
+                    shared_intermediate: int = 0):
     """Seeded N(0, std) MoE layer quantized like compress_layer_state_dict
     (src/quantization.rs:278-312: tensors with >= 4096 elements are quantized).
     Returns (MoeWeights, dict of float32 originals)."""

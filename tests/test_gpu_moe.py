@@ -81,6 +81,7 @@ CASES = [
     (300, 256, 256, 4, 2, 2, True),    # N tile widths 128/64/32/16 across experts
     (9, 256, 256, 8, 2, 1, False),
     (40, 512, 256, 8, 4, 2, False),
+    (8, 2048, 768, 128, 8, 1, True),   # fine-grained: 128 experts, top-8 (many 16-wide N tiles)
 ]
 
 
