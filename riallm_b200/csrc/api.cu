@@ -2,9 +2,11 @@
 //
 // Orchestrates one MoE block call (src/model.rs:751-818) as a fixed sequence
 // of launches on the caller's stream, with no host synchronisation:
-//   dequant router weights -> router/top-k -> counting-sort permutation ->
-//   gather tokens -> expert GEMMs (tcgen05 for bf16 activations, CUDA cores
-//   for float32) -> [shared expert] -> weighted combine.
+//   router (router weight decoded on the fly, softmax, stable top-k, and the
+//   counting sort of the token-expert pairs in its last CTA) -> gather
+//   tokens -> expert GEMMs (tcgen05 for bf16 activations, CUDA cores for
+//   float32) -> [shared expert] -> weighted combine. The small kernels and
+//   the tcgen05 GEMMs use programmatic dependent launch.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
