@@ -1,8 +1,8 @@
 """CPU oracle for riallm's block quantization and MoE block forward.
 
 TEST INFRASTRUCTURE ONLY. Only tests/, __graft_entry__.smoke() and bench.py's
-cpu_baseline / reference arm import this module, as the checker or the timed
-CPU port. The product (riallm_b200) never imports it.
+cpu_baseline / reference arm import this module, as the parity reference or
+the timed CPU port. The product (riallm_b200) never imports it.
 
 PARITY UNPINNED: the reference (Rust, candle 0.8) cannot be built or run
 here and its tests pin no values (tests/integration_test.rs:124-148). The C

@@ -1,7 +1,7 @@
 /*
  * riallm_oracle.c -- CPU restatement of riallm's block quantization and MoE
- * block forward. TEST INFRASTRUCTURE ONLY (the checker and the timed CPU
- * port); the product never links it. PARITY UNPINNED: see riallm_oracle.h.
+ * block forward. TEST INFRASTRUCTURE ONLY (the parity reference and the
+ * timed CPU port); the product never links it. PARITY UNPINNED: see riallm_oracle.h.
  *
  * Build: oracle/Makefile (gcc -O2 -fopenmp -ffp-contract=off). Contraction
  * must stay off: every rounding step below is meant literally.

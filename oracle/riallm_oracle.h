@@ -5,7 +5,7 @@
  * TEST INFRASTRUCTURE ONLY. Nothing in the product (riallm_b200/, the CUDA
  * library, bench.py's GPU arms) links or calls this code; only tests/,
  * __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm use it,
- * and only as the checker or as the timed CPU port.
+ * and only as the parity reference or as the timed CPU port.
  *
  * PARITY UNPINNED: the reference is Rust (candle 0.8) and cannot be built or
  * run in this environment (no cargo/rustc, no network), and its own tests
