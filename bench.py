@@ -146,12 +146,12 @@ def run_reference(args, rank, world):
     t1 = time.perf_counter()
     O.moe_forward(w, x[:1], 1, H, I, E, TOP_K, n_threads=threads)
     one_token_s = time.perf_counter() - t1
-    budget_s = 150.0
+    max_run_s = 150.0
     n_calls = args.warmup + args.steps
     sample_tokens = args.tokens
     est = n_calls * one_token_s * sample_tokens * 0.6  # tokens share dequantized rows
-    if est > budget_s:
-        sample_tokens = max(1, int(args.tokens * budget_s / est))
+    if est > max_run_s:
+        sample_tokens = max(1, int(args.tokens * max_run_s / est))
     xs = x[:sample_tokens]
     for _ in range(args.warmup):
         O.moe_forward(w, xs, sample_tokens, H, I, E, TOP_K, n_threads=threads)
