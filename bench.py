@@ -16,7 +16,9 @@ all-gathers the ranks' batches (NCCL), runs its experts for all tokens and
 reduce-scatters the partial sums (weak scaling: 64 tokens per GPU); value
 is the total tokens of all ranks over the slowest rank's device time.
 The single-GPU line also carries a Mixtral-8x7B decode measurement (32
-layers, batch 1 and 32; --decode-only runs it alone).
+layers, batch 1 and 32; --decode-only runs it alone), a token-count sweep,
+the fine-grained block (128 experts, top-8) and layer streaming from pinned
+host memory for the Mixtral-8x7B block and a Mixtral-8x22B-shaped one.
 
 --impl reference times the oracle's CPU port of riallm's MoE block
 (oracle/riallm_oracle.c, all host threads) on the same workload; the Rust
@@ -187,19 +189,20 @@ def config_dict(args, world):
 
 # ------------------------------------------------------------------ ours
 
-def make_layer(rb, torch, device, seed=2):
-    """Seeded N(0, 0.02) weights quantized to NF4 in riallm's layout. Each
-    tensor is generated and quantized one expert slice at a time into the
-    full tensor's buffers (64-element blocks never straddle experts, so the
-    bytes, scales and zero points equal those of quantizing the whole tensor
-    at once); this keeps the device footprint near the 0.9 GB of NF4 data."""
-    import ctypes as C
+def make_layer(rb, torch, device, seed=2, hidden=H, inter=I, experts=E):
+    """Seeded N(0, 0.02) weights quantized to NF4 in riallm's layout (the
+    Mixtral-8x7B block by default). Each tensor is generated and quantized
+    one expert slice at a time into the full tensor's buffers (64-element
+    blocks never straddle experts, so the bytes, scales and zero points equal
+    those of quantizing the whole tensor at once); this keeps the device
+    footprint near the NF4 data (0.9 GB for Mixtral-8x7B)."""
     gen = torch.Generator(device=device).manual_seed(seed)
     L = rb.lib()
     ctx = rb.Context.get(device.index or 0)
     d = {}
-    for name, shape in (("mlp.gate.weight", (E, H)), ("mlp.experts.gate_up_proj", (E, 2 * I, H)),
-                        ("mlp.experts.down_proj", (E, H, I))):
+    for name, shape in (("mlp.gate.weight", (experts, hidden)),
+                        ("mlp.experts.gate_up_proj", (experts, 2 * inter, hidden)),
+                        ("mlp.experts.down_proj", (experts, hidden, inter))):
         numel = 1
         for v in shape:
             numel *= v
@@ -451,7 +454,8 @@ def run_ours(args, rank, world, local):
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
         cpu = cpu_baseline(rb, torch, d, blk)
-    streaming = None if args.no_stream else stream_measure(rb, torch, d, blk)
+    streaming = None if args.no_stream else stream_measure(rb, torch, d, blk.x)
+    streaming_8x22b = None if args.no_stream else stream_measure_8x22b(rb, torch, device)
     decode = None if args.no_decode else decode_measure(rb, torch, device, decode_batches(args),
                                                         new_tokens=args.decode_new)
     fine = None if args.no_sweep else fine_grained_measure(rb, torch, device)
@@ -467,7 +471,8 @@ def run_ours(args, rank, world, local):
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": f"{launches_per_step} kernels per step (router, gather, expert gate_up and down GEMMs, combine) replayed from one CUDA graph",
             "captured_launches": per_step_launches,
-            "clocks": clk.summary(), "sweep": sweep, "streaming": streaming, "decode": decode, "fine_grained": fine,
+            "clocks": clk.summary(), "sweep": sweep, "streaming": streaming, "streaming_8x22b": streaming_8x22b,
+            "decode": decode, "fine_grained": fine,
         }
         print(json.dumps(line), flush=True)
     del g
@@ -604,20 +609,19 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     return 0
 
 
-def stream_measure(rb, torch, d, blk, n_layers=4, depth=2):
-    """Streaming mode (ModelOptions.prefetch_layers): the block's NF4 layer
+def stream_measure(rb, torch, d, x, n_layers=4, depth=2, experts=E, top_k=TOP_K, label=None):
+    """Streaming mode (ModelOptions.prefetch_layers): one NF4 MoE layer
     packed once into pinned host memory and streamed through a ring of
     `depth` device slots, n_layers layers per pass (the same layer bytes
-    n_layers times), one 64-token decode batch per layer. Reports the H2D
-    rate of the copies and how much of the copy time the compute hides."""
+    n_layers times), the decode batch `x` through each layer. Reports the
+    H2D rate of the copies and how much of the copy time the compute hides."""
     from riallm_b200.streaming import LayerStreamer, PackedLayer
     packed = PackedLayer({k: v for k, v in d.items()})
     layers = [packed] * n_layers
-    s = LayerStreamer(layers, depth=depth, device=blk.x.device.index or 0)
-    x = blk.x
+    s = LayerStreamer(layers, depth=depth, device=x.device.index or 0)
 
     def fn(i, t):
-        rb.apply_moe(t, x, TOP_K, E)
+        rb.apply_moe(t, x, top_k, experts)
     s.run(fn)  # warm-up pass
     torch.cuda.synchronize()
     b0 = s.stats()
@@ -634,19 +638,39 @@ def stream_measure(rb, torch, d, blk, n_layers=4, depth=2):
     nbytes = (b1["bytes"] - b0["bytes"]) / passes
     start.record()
     for _ in range(passes * n_layers):
-        rb.apply_moe(d, x, TOP_K, E)
+        rb.apply_moe(d, x, top_k, experts)
     end.record()
     torch.cuda.synchronize()
     compute = start.elapsed_time(end) / passes
     s.close()
     packed.close()
-    return {"layers_per_pass": n_layers, "prefetch_buffer_size": depth, "layer_bytes": packed.nbytes,
-            "ms_per_pass": round(wall, 3), "h2d_gbs": round(nbytes / (copy_ms / 1000.0) / 1e9, 2),
-            "h2d_gbs_wall": round(nbytes / (wall / 1000.0) / 1e9, 2),
-            "compute_ms_per_pass": round(compute, 3),
-            "exposed_copy_ms_per_pass": round(max(wall - compute, 0.0), 3),
-            "tokens_per_s": round(x.shape[0] / (wall / 1000.0), 1),
-            "note": "pinned host -> HBM over PCIe on a copy stream; copies of layers i+1 overlap layer i's block"}
+    out = {"layers_per_pass": n_layers, "prefetch_buffer_size": depth, "layer_bytes": packed.nbytes,
+           "tokens_per_layer": x.shape[0],
+           "ms_per_pass": round(wall, 3), "h2d_gbs": round(nbytes / (copy_ms / 1000.0) / 1e9, 2),
+           "h2d_gbs_wall": round(nbytes / (wall / 1000.0) / 1e9, 2),
+           "compute_ms_per_pass": round(compute, 3),
+           "exposed_copy_ms_per_pass": round(max(wall - compute, 0.0), 3),
+           "tokens_per_s": round(x.shape[0] / (wall / 1000.0), 1),
+           "note": "pinned host -> HBM over PCIe on a copy stream; copies of layers i+1 overlap layer i's block"}
+    if label:
+        out = {"layer": label, **out}
+    return out
+
+
+def stream_measure_8x22b(rb, torch, device, n_layers=2, tokens=16, seed=5):
+    """The streaming measurement on a Mixtral-8x22B-shaped layer (hidden
+    6144, intermediate 16384, 8 experts, top-2; N(0, 0.02) weights seed 5
+    quantized to NF4, 1.57 GB per layer) with a 16-token decode batch."""
+    h, inter = 6144, 16384
+    d = make_layer(rb, torch, device, seed=seed, hidden=h, inter=inter, experts=E)
+    gen = torch.Generator(device=device).manual_seed(seed + 1)
+    x = torch.empty(tokens, h, device=device).normal_(0, 1, generator=gen).to(torch.bfloat16)
+    out = stream_measure(rb, torch, d, x, n_layers=n_layers,
+                         label="mixtral-8x22b block (H 6144, I 16384, E 8, top-2, NF4)")
+    del d
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
 
 
 def decode_batches(args):
@@ -718,26 +742,44 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
     return out
 
 
+def zipf_bias(torch, n, s=1.1, seed=4):
+    """Expert-popularity bias of the fine-grained configuration:
+    bias_e = ln(r_e^-s / sum_r r^-s), the ranks r_e = 1..n given to the
+    experts by a seeded permutation (torch CPU generator)."""
+    g = torch.Generator().manual_seed(seed)
+    ranks = torch.randperm(n, generator=g).double() + 1.0
+    w = ranks ** -s
+    return torch.log(w / w.sum()).float()
+
+
 def fine_grained_measure(rb, torch, device, steps=20):
     """The fine-grained MoE configuration (hidden 2048, 128 experts, top-8,
     intermediate 768; N(0, 0.02) weights, seed 4): a 64-token decode batch
-    with NF4 and with 8-bit experts, and an 8192-token prefill with NF4.
-    Expert-GEMM time from the library's phase events; one block call per
-    step."""
-    import ctypes as C
+    with NF4 and with 8-bit experts, an 8192-token prefill with NF4, and a
+    64-token NF4 decode batch whose router logits carry a Zipf(1.1)
+    expert-popularity bias. The router has no bias input, so the bias rides
+    on the last hidden feature: it is set to 1 in every token and the
+    router's last column holds the bias; that router stays float32 (a
+    quantized one would lose the bias to the block's absmax). Expert-GEMM
+    time from the library's phase events; one block call per step."""
     Hf, If, Ef, kf = 2048, 768, 128, 8
-    L = rb.lib()
     ctx = rb.Context.get(device.index or 0)
     hbm_peak, bf16_peak, _, _ = load_peaks()
     out = {"config": "fine-grained: hidden 2048, 128 experts, top-8, intermediate 768", "runs": []}
-    for qt, T in ((rb.CompressionType.FourBit, 64), (rb.CompressionType.EightBit, 64),
-                  (rb.CompressionType.FourBit, 8192)):
+    for qt, T, zipf in ((rb.CompressionType.FourBit, 64, False), (rb.CompressionType.EightBit, 64, False),
+                        (rb.CompressionType.FourBit, 8192, False), (rb.CompressionType.FourBit, 64, True)):
         g = torch.Generator(device=device).manual_seed(4)
-        d = {"mlp.gate.weight": rb.quantize_tensor(torch.randn(Ef, Hf, device=device, generator=g) * 0.02, qt),
+        wg = torch.randn(Ef, Hf, device=device, generator=g) * 0.02
+        if zipf:
+            wg[:, Hf - 1] = zipf_bias(torch, Ef).to(device)
+        d = {"mlp.gate.weight": wg if zipf else rb.quantize_tensor(wg, qt),
              "mlp.experts.gate_up_proj": rb.quantize_tensor(
                  torch.randn(Ef, 2 * If, Hf, device=device, generator=g) * 0.02, qt),
              "mlp.experts.down_proj": rb.quantize_tensor(torch.randn(Ef, Hf, If, device=device, generator=g) * 0.02, qt)}
-        x = torch.randn(T, Hf, device=device, generator=g).to(torch.bfloat16)
+        x = torch.randn(T, Hf, device=device, generator=g)
+        if zipf:
+            x[:, Hf - 1] = 1.0
+        x = x.to(torch.bfloat16)
         counts = rb.route(d["mlp.gate.weight"], x, kf, Ef)[2]
         U = int((counts > 0).sum().item())
         for _ in range(3):
@@ -747,7 +789,10 @@ def fine_grained_measure(rb, torch, device, steps=20):
         kern_ms = ph["gate_up"] + ph["down"]
         bpw = 0.625 if qt == rb.CompressionType.FourBit else 1.0 + 8.0 / 128.0
         run = {"qtype": qt.name, "tokens": T, "tokens_per_s": round(T * steps / (ms / 1000.0), 1),
-               "ms_per_step": round(ms / steps, 4), "distinct_experts": U, "kernel_ms": round(kern_ms, 4)}
+               "ms_per_step": round(ms / steps, 4), "distinct_experts": U,
+               "max_pairs_per_expert": int(counts.max().item()), "kernel_ms": round(kern_ms, 4)}
+        if zipf:
+            run["router"] = "float32 with a Zipf(1.1) expert-popularity bias"
         if T <= 512:
             bytes_step = U * 3 * Hf * If * bpw
             gbs = bytes_step / (kern_ms / 1000.0) / 1e9

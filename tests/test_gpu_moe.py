@@ -82,6 +82,7 @@ CASES = [
     (9, 256, 256, 8, 2, 1, False),
     (40, 512, 256, 8, 4, 2, False),
     (8, 2048, 768, 128, 8, 1, True),   # fine-grained: 128 experts, top-8 (many 16-wide N tiles)
+    (4, 6144, 512, 8, 2, 1, True),     # Mixtral-8x22B hidden size (K = 6144 in gate_up)
 ]
 
 
