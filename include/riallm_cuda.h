@@ -233,7 +233,8 @@ int32_t riallm_cuda_moe_route(riallm_ctx* ctx, const riallm_qtensor* gate,
  * RIALLM_ERR_MEMORY without launching anything. The first call on each
  * device looks up the array's device address (and sets kernel attributes);
  * make that first call before any stream capture. Every call reuses the same
- * array and leaves its contents behind, so calls that overlap on the GPU
+ * array and leaves its contents behind (the counters that must start at zero
+ * are cleared at the start of every call), so calls that overlap on the GPU
  * (other streams or host threads) race on it: serialize them. Runs on the
  * current CUDA device and on `stream`. */
 int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, const void* x,

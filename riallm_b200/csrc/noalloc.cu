@@ -113,12 +113,15 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* base = reinterpret_cast<char*>(slot->scratch);
   const int P = T * k;
-  // Only the status word must be zeroed per call. The counters in the
-  // layout's first bytes (the router's completion counter, the expert
-  // GEMM's split-tile counters) start at zero with the array and every call
-  // returns them to zero. Every other buffer is fully written before it is
+  // The status word and the counters in the layout's first kSyncBytes (the
+  // router's completion counter, the expert GEMM's split-tile counters) must
+  // read zero when the call starts. A completed call leaves them at zero, but
+  // one that stopped early (an expired device wait) may not, so both are
+  // cleared on every call. Every other buffer is fully written before it is
   // read within the call.
-  if (cudaMemsetAsync(slot->status, 0, sizeof(int), st) != cudaSuccess) return RIALLM_ERR_CUDA;
+  if (cudaMemsetAsync(slot->status, 0, sizeof(int), st) != cudaSuccess ||
+      cudaMemsetAsync(base + L.sync, 0, rl::kSyncBytes, st) != cudaSuccess)
+    return RIALLM_ERR_CUDA;
   int* topk_idx = reinterpret_cast<int*>(base + L.topk_idx);
   float* topk_w = reinterpret_cast<float*>(base + L.topk_w);
   int* counts = reinterpret_cast<int*>(base + L.counts);
