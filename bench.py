@@ -844,7 +844,8 @@ def cpu_baseline(rb, torch, d, blk):
                       f"(oracle/riallm_oracle.c, OpenMP), same NF4 weights"}
 
 
-def main():
+def parse_args(argv=None):
+    """Command-line options; fewer than 3 warm-up steps are raised to 3."""
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -859,9 +860,14 @@ def main():
                     help="run only the Mixtral-8x7B decode measurement and print its JSON")
     ap.add_argument("--decode-batches", default="1,32", help="batch sizes of the decode measurement")
     ap.add_argument("--decode-new", type=int, default=128, help="decode steps per batch size")
-    args = ap.parse_args()
+    args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3
+    return args
+
+
+def main():
+    args = parse_args()
     rank, world, local = dist_setup()
     if args.impl == "reference":
         return run_reference(args, rank, world)
