@@ -6,7 +6,8 @@
 //   counting sort of the token-expert pairs in its last CTA) -> gather
 //   tokens -> expert GEMMs (tcgen05 for bf16 activations, CUDA cores for
 //   float32) -> [shared expert] -> weighted combine. The small kernels and
-//   the tcgen05 GEMMs use programmatic dependent launch.
+//   the tcgen05 GEMMs use programmatic dependent launch, and at decode sizes
+//   the gate_up GEMM prefetches the down GEMM's first weight stages into L2.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -508,11 +509,6 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     g.sk_ws = L.sk_ws ? (float*)(base + L.sk_ws) : nullptr;
     g.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
     g.pdl = true;  // follows the gather
-    {
-      PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
-      RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
-      ctx->launches += 1;
-    }
     rl::TcGemmArgs d{};
     d.w = w->down_proj;
     d.K = I;
@@ -533,6 +529,12 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     d.sk_ws = L.sk_ws ? (float*)(base + L.sk_ws) : nullptr;
     d.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
     d.pdl = true;  // follows the gate_up GEMM
+    g.next = &d;  // gate_up prefetches the down launch's first weight stages
+    {
+      PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
+      RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
+      ctx->launches += 1;
+    }
     {
       PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
       RL_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");

@@ -119,6 +119,9 @@ struct Params {
   int d_cols;     // 64 or 128 accumulator columns per operand
   float* sk_ws;   // split-tile partial sums, one [2][d_cols][128] f32 slot per CTA; null: whole tiles
   int* sk_flags;  // one counter per CTA, zero between launches
+  // The next launch's shape, for the L2 prefetch of its first stages
+  // (pf_K == 0: no prefetch).
+  int pf_K, pf_rows_per_expert, pf_a1_offset, pf_m_step, pf_m_tiles, pf_sk;
 };
 
 struct Tile {
@@ -380,6 +383,63 @@ __device__ __forceinline__ void issue_stage(uint32_t d, uint32_t a_k, uint64_t b
   }
 }
 
+// Raw stages of the next launch prefetched into L2 per CTA.
+constexpr int kPfStages = 2;
+
+// The next expert GEMM launch (same weight format) starts on SMs as this
+// launch's CTAs exit, and its first weight bytes then come from HBM after
+// its prologue. This CTA's producer, once its own loads are all issued,
+// works out the first item the same CTA index gets in the next launch (the
+// same schedule as Sched over that launch's tiles: ntn is shared, since
+// both launches tile the same pairs) and prefetches that item's first
+// kPfStages raw stages -- codes and, for NF4, scales and zero points --
+// into L2. A prefetch only warms the cache; results do not depend on it.
+template <bool kNF4, int KR, int PPS>
+__device__ __forceinline__ void prefetch_next_launch(const Params& p, const int* ntn,
+                                                     const CUtensorMap* raw, const CUtensorMap* scl,
+                                                     const CUtensorMap* zer) {
+  const int n_raw = p.pf_K / KR;
+  int total = 0;
+  for (int e = 0; e < p.E; ++e) total += ntn[e] * p.pf_m_tiles;
+  if (total == 0 || n_raw == 0) return;
+  const int G = gridDim.x, b = blockIdx.x;
+  const int rounds = total / G >= 2 ? total / G - 1 : 0;
+  const int sk_tile0 = p.pf_sk ? rounds * G : total;
+  int t, r0;
+  if (b < sk_tile0) {
+    t = b;
+    r0 = 0;
+  } else {
+    const uint64_t W = (uint64_t)(total - sk_tile0) * n_raw;
+    const uint64_t w = W * b / G, w1 = W * (b + 1) / G;
+    if (w >= w1) return;
+    const int lt = (int)(w / (uint64_t)n_raw);
+    t = sk_tile0 + lt;
+    r0 = (int)(w - (uint64_t)lt * n_raw);
+  }
+  int e = 0, start = 0;
+  for (; e < p.E; ++e) {
+    const int n = ntn[e] * p.pf_m_tiles;
+    if (t < start + n) break;
+    start += n;
+  }
+  if (e >= p.E) return;
+  const int m_idx = (t - start) / ntn[e];
+  const int row0 = e * p.pf_rows_per_expert + m_idx * p.pf_m_step;
+  const int row1 = row0 + p.pf_a1_offset;
+  const int r1 = min(n_raw, r0 + kPfStages);
+  for (int c = r0; c < r1; ++c) {
+    tma_prefetch_l2_2d(raw, c * 128, row0);
+    tma_prefetch_l2_2d(raw, c * 128, row1);
+    if (kNF4) {
+      tma_prefetch_l2_2d(scl, c * PPS, row0);
+      tma_prefetch_l2_2d(zer, c * PPS, row0);
+      tma_prefetch_l2_2d(scl, c * PPS, row1);
+      tma_prefetch_l2_2d(zer, c * PPS, row1);
+    }
+  }
+}
+
 template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tm_raw,
@@ -388,7 +448,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap tm_b16,
                        const __grid_constant__ CUtensorMap tm_b32,
                        const __grid_constant__ CUtensorMap tm_b64,
-                       const __grid_constant__ CUtensorMap tm_b128, const Params p) {
+                       const __grid_constant__ CUtensorMap tm_b128,
+                       const __grid_constant__ CUtensorMap tm_nraw,
+                       const __grid_constant__ CUtensorMap tm_nscl,
+                       const __grid_constant__ CUtensorMap tm_nzer, const Params p) {
   constexpr bool kNF4 = QT == RIALLM_COMPRESSION_FOUR_BIT;
   constexpr int KR = kNF4 ? 256 : 128;  // K per raw stage (128 code bytes per row)
   constexpr int AS_PER_RAW = KR / 128;  // A stages (128 K each) per raw stage
@@ -530,6 +593,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (ok && p.pf_K > 0) prefetch_next_launch<kNF4, KR, PPS>(p, ntn, &tm_nraw, &tm_nscl, &tm_nzer);
       // Drain: every issued copy lands before the CTA can exit.
       for (uint32_t j = (it > (uint32_t)n_rs ? it - n_rs : 0); j < it; ++j)
         wait_drain(&raw_full[j % n_rs], (j / n_rs) & 1);
@@ -942,28 +1006,44 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace tc
 
-cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream) {
-  if (a.P == 0) return cudaSuccess;
+// Tensor maps of a launch's weights: the packed codes (128 rows x 128 bytes
+// per box, 128-byte swizzle) and, for NF4, the scales and zero points
+// viewed as [rows, K/64] float32 (K % 256 == 0 keeps the 16-byte row
+// stride; a stage reads a 4-block x 128-row box). For 8-bit weights the
+// parameter maps are copies of the code map and are not used.
+static bool encode_weight_maps(const TcGemmArgs& a, CUtensorMap* raw, CUtensorMap* scl, CUtensorMap* zer) {
   const bool nf4 = a.w.qtype == RIALLM_COMPRESSION_FOUR_BIT;
   const uint64_t row_bytes = nf4 ? (uint64_t)a.K / 2 : (uint64_t)a.K;
   const uint64_t total_rows = (uint64_t)a.E * a.rows_per_expert;
-  CUtensorMap tm_raw, tm_scl, tm_zer, tm_b[4];
-  if (encode_tensor_map_2d(&tm_raw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w.data, row_bytes, total_rows,
+  if (encode_tensor_map_2d(raw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w.data, row_bytes, total_rows,
                            row_bytes, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
-    return cudaErrorInvalidValue;
-  if (nf4) {
-    // Scales / zero points viewed as [rows, K/64] float32 (K % 256 == 0 keeps
-    // the 16-byte row stride); a stage reads a 4-block x 128-row box.
-    const uint64_t bpr = (uint64_t)a.K / 64;
-    if (encode_tensor_map_2d(&tm_scl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.w.scales, bpr, total_rows, bpr * 4,
-                             4, 128, CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS ||
-        encode_tensor_map_2d(&tm_zer, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.w.zero_points, bpr, total_rows,
-                             bpr * 4, 4, 128, CU_TENSOR_MAP_SWIZZLE_NONE) != CUDA_SUCCESS)
-      return cudaErrorInvalidValue;
-  } else {
-    tm_scl = tm_raw;
-    tm_zer = tm_raw;
+    return false;
+  if (!nf4) {
+    *scl = *raw;
+    *zer = *raw;
+    return true;
   }
+  const uint64_t bpr = (uint64_t)a.K / 64;
+  return encode_tensor_map_2d(scl, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.w.scales, bpr, total_rows, bpr * 4, 4,
+                              128, CU_TENSOR_MAP_SWIZZLE_NONE) == CUDA_SUCCESS &&
+         encode_tensor_map_2d(zer, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.w.zero_points, bpr, total_rows, bpr * 4,
+                              4, 128, CU_TENSOR_MAP_SWIZZLE_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream) {
+  if (a.P == 0) return cudaSuccess;
+  const bool nf4 = a.w.qtype == RIALLM_COMPRESSION_FOUR_BIT;
+  CUtensorMap tm_raw, tm_scl, tm_zer, tm_b[4];
+  if (!encode_weight_maps(a, &tm_raw, &tm_scl, &tm_zer)) return cudaErrorInvalidValue;
+  // The next launch's weights, prefetched at this launch's tail when they
+  // have the same format (the kernel variant is per format) and tiles are
+  // decode-sized (<= 64 pairs), where a launch's start-up latency is a
+  // visible share of its time.
+  const TcGemmArgs* nx = a.next;
+  const bool pf = nx != nullptr && nx->w.qtype == a.w.qtype && nx->E == a.E && nx->P == a.P &&
+                  nx->counts == a.counts && a.max_pairs_per_expert <= 64;
+  CUtensorMap tm_nraw = tm_raw, tm_nscl = tm_scl, tm_nzer = tm_zer;
+  if (pf && !encode_weight_maps(*nx, &tm_nraw, &tm_nscl, &tm_nzer)) return cudaErrorInvalidValue;
   const uint32_t Ns[4] = {16, 32, 64, 128};
   for (int i = 0; i < 4; ++i)
     if (encode_tensor_map_2d(&tm_b[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.b, (uint64_t)a.K,
@@ -973,7 +1053,9 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
   tc::Params p{a.w.scales, a.w.zero_points, a.w.n_scales, a.w.n_zero_points, a.K,
                a.rows_per_expert, a.a1_offset, a.m_step, a.m_tiles, a.counts, a.offsets, a.E,
                a.swiglu ? 1 : 0, a.h_pair_perm ? 1 : 0, a.h_out, a.y_out, a.ld_out, a.status,
-               a.max_pairs_per_expert <= 64 ? 64 : 128, a.sk_ws, a.sk_flags};
+               a.max_pairs_per_expert <= 64 ? 64 : 128, a.sk_ws, a.sk_flags,
+               pf ? nx->K : 0, pf ? nx->rows_per_expert : 0, pf ? nx->a1_offset : 0,
+               pf ? nx->m_step : 0, pf ? nx->m_tiles : 0, pf && nx->sk_ws != nullptr ? 1 : 0};
   auto kern = nf4 ? tc::expert_gemm_kernel<RIALLM_COMPRESSION_FOUR_BIT>
                   : tc::expert_gemm_kernel<RIALLM_COMPRESSION_EIGHT_BIT>;
   // Set the shared-memory opt-in once per device and variant, outside any
@@ -997,7 +1079,8 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.pdl ? 1 : 0;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tm_raw, tm_scl, tm_zer, tm_b[0], tm_b[1], tm_b[2], tm_b[3], p);
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tm_raw, tm_scl, tm_zer, tm_b[0], tm_b[1], tm_b[2], tm_b[3], tm_nraw,
+                                       tm_nscl, tm_nzer, p);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }

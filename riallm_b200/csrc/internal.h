@@ -165,6 +165,13 @@ struct TcGemmArgs {
   // produce the routing counts) is still running; token tiles, outputs and
   // the split-tile workspace are touched only after griddepcontrol.wait.
   bool pdl;
+  // The expert GEMM launched right after this one on the same stream (the
+  // down projection after gate_up), or null. When its weights have this
+  // launch's format and tiles are decode-sized (<= 64 pairs per expert),
+  // each CTA, once it has issued its last weight loads,
+  // prefetches into L2 the first weight stages that the same CTA index
+  // reads in the next launch.
+  const TcGemmArgs* next = nullptr;
 };
 // Bytes of the split-tile workspace of launch_tc_gemm: one slot of
 // 2 operands x 128 rows x (64 or 128) f32 columns per CTA (= per SM).
