@@ -256,9 +256,11 @@ def expert_bytes(T, U):
 
 
 # DRAM bytes of one step's two expert-GEMM launches (read + written), from
-# one ncu capture of the 64-token workload: 604.9 + 6.8 MB (gate_up) and
-# 317.4 + 6.4 MB (down), against 891.3 MB algorithmic.
-TRAFFIC_T64 = 935.5e6
+# one ncu capture of the 64-token workload: 625.7 + 10.0 MB (gate_up) and
+# 317.9 + 6.4 MB (down), against 891.3 MB algorithmic. ncu flushes the
+# caches between kernels, so the down launch's first stages, which gate_up
+# prefetches into L2, are counted twice there (~12 MB).
+TRAFFIC_T64 = 960.0e6
 
 
 def expert_flops(T):
