@@ -30,7 +30,9 @@
 //
 // Scheduling: whole tiles round-robin over the CTAs while two or more full
 // waves remain, then stream-K shares of the rest (see Sched), so all SMs
-// stream the same number of weight bytes.
+// stream the same number of weight bytes. At decode sizes the gate_up
+// launch's producer, after its last load, prefetches into L2 the first
+// stages of the down launch that follows (prefetch_next_launch).
 //
 // NF4 scales and zero points ride in the same TMA stage as the codes (a
 // 128-row x 4-block box of each); 8-bit ones are fetched by the dequant
