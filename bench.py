@@ -588,6 +588,7 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     tt = torch.tensor([t0.elapsed_time(t1)], device="cuda")
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     e2e_ms = float(tt.item())
+    ep_check = ep_verify(rb, torch, dist, d, blk, x, rank, world)
     nbytes = x.numel() * 2
     e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
@@ -603,12 +604,31 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
             "roofline": roofline, "cpu_baseline": None, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
             "gpu_launches_note": f"{launches_per_step} library kernels per step per GPU (router, gather, expert gate_up and down GEMMs, partial combine) plus NCCL all-gather and reduce-scatter",
-            "clocks": clk.summary(), "sweep": [],
+            "clocks": clk.summary(), "sweep": [], "ep_check": ep_check,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
-    return 0
+    return 0 if ep_check["passed"] else 1
+
+
+EP_TOL = 5e-3
+
+
+def ep_verify(rb, torch, dist, d, blk, x, rank, world):
+    """Checks the expert-parallel step's output on every rank against the
+    single-GPU block run on the same gathered tokens (this rank holds the
+    whole layer): max |ep - single| / max |single| over each rank's tokens
+    within EP_TOL; the worst rank's error is reported."""
+    out = blk(x)
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x)
+    ref = rb.apply_moe(d, torch.cat(parts, 0), TOP_K, E)[rank * x.shape[0]:(rank + 1) * x.shape[0]]
+    err = ((out.float() - ref.float()).abs().max() / ref.float().abs().max()).reshape(1)
+    dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    e = float(err.item())
+    return {"max_rel_err": e, "tol": EP_TOL, "passed": e < EP_TOL,
+            "against": "single-GPU riallm_cuda_moe_forward on the same gathered tokens, every rank"}
 
 
 def stream_measure(rb, torch, d, x, n_layers=4, depth=2, experts=E, top_k=TOP_K, label=None):

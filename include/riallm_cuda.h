@@ -227,20 +227,30 @@ int32_t riallm_cuda_moe_route(riallm_ctx* ctx, const riallm_qtensor* gate,
  * from one 24 MiB array compiled into the library, which every GPU that
  * loads the library holds until the process exits. Nothing is allocated.
  * Limits: bf16 x/out ([T,H], 16-byte aligned), routed experts only (no
- * shared expert), the same shape rules as riallm_cuda_moe_forward, and the
- * call's scratch layout must fit 24 MiB (for hidden 4096 / intermediate
- * 14336, up to 472 token-expert pairs, T*k); larger calls return
- * RIALLM_ERR_MEMORY without launching anything. The first call on each
- * device looks up the array's device address (and sets kernel attributes);
- * make that first call before any stream capture. Every call reuses the same
- * array and leaves its contents behind (the counters that must start at zero
- * are cleared at the start of every call), so calls that overlap on the GPU
- * (other streams or host threads) race on it: serialize them. Runs on the
- * current CUDA device and on `stream`. */
+ * shared expert), the same shape rules and argument checks (with the same
+ * status codes) as riallm_cuda_moe_forward, and the call's scratch layout
+ * must fit 24 MiB (for hidden 4096 / intermediate 14336, up to 472
+ * token-expert pairs, T*k); larger calls return RIALLM_ERR_MEMORY without
+ * launching anything. The first call on each device looks up the array's
+ * device address (and sets kernel attributes); make that first call before
+ * any stream capture (a look-up that fails is retried by the next call).
+ * Every call reuses the same array and leaves its contents behind (the
+ * counters that must start at zero are cleared at the start of every call),
+ * so calls that overlap on the GPU (other streams or host threads) race on
+ * it: serialize them. Runs on the current CUDA device and on `stream`. A
+ * RIALLM_OK return means the work was queued; whether it completed cleanly
+ * is reported by riallm_cuda_moe_forward_noalloc_sync. */
 int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, const void* x,
                                         void* out, int32_t T, int32_t H, int32_t I,
                                         int32_t E, int32_t k, uint32_t flags,
                                         void* stream);
+
+/* No counterpart in the reference. Waits for `stream`, then reports whether
+ * every riallm_cuda_moe_forward_noalloc call on the current device since the
+ * last report ran to completion: RIALLM_OK, or RIALLM_ERR_TIMEOUT when a
+ * bounded device-side wait expired in one of them (the `out` of such a call
+ * is undefined). The record is cleared by reading it. Allocates nothing. */
+int32_t riallm_cuda_moe_forward_noalloc_sync(void* stream);
 
 /* ---------------------------------------------------------- profiling
  * The reference's Profiler (src/profiler.rs:75-96) times each layer on the

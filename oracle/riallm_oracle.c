@@ -418,7 +418,10 @@ void ro_moe_forward(const ro_moe_weights* w, const void* x, int32_t act_bf16,
     for (int32_t j = 0; j < n; ++j) {
       int32_t pr = perm[off[e] + j];
       int32_t tok = pr / k;
-      float wt = tw[pr];
+      /* src/model.rs:800-802: the routing weight is cast to the activation
+       * dtype before it scales the expert output (bf16 rounding in bf16
+       * mode); the product and the sum stay float32. */
+      float wt = act_bf16 ? round_bf16(tw[pr]) : tw[pr];
       float* o = out + (uint64_t)tok * H;
       const float* yv = y + (uint64_t)j * H;
       for (int32_t h = 0; h < H; ++h) o[h] = o[h] + yv[h] * wt;

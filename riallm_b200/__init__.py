@@ -114,6 +114,7 @@ SIGNATURES = {
     "riallm_cuda_launch_count": (_u64, [_vp]),
     "riallm_cuda_moe_forward_noalloc": (_i32, [ctypes.POINTER(CMoeWeights), _vp, _vp, _i32, _i32, _i32,
                                                _i32, _i32, _u32, _vp]),
+    "riallm_cuda_moe_forward_noalloc_sync": (_i32, [_vp]),
     "riallm_cuda_moe_forward_ep": (_i32, [_vp, ctypes.POINTER(CMoeWeights), _vp, _vp, _i32, _i32, _i32,
                                           _i32, _i32, _i32, _i32, _vp]),
     "riallm_cuda_streamer_create": (_i32, [_vp, _i32, _u64, _vp, ctypes.POINTER(_vp)]),

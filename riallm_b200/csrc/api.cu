@@ -631,7 +631,8 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     PhaseScope ps(ctx, st, RIALLM_PHASE_COMBINE);
     RL_CUDA(ctx, rl::launch_combine((const float*)(base + L.y_perm), (const int*)(base + L.inv_pos),
                                     (const int*)(base + L.topk_idx), (const float*)(base + L.topk_w), T, k, H,
-                                    shared_y, shared_gate, out, bf16, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st),
+                                    shared_y, shared_gate, out, bf16, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st,
+                                    0, 1 << 30, bf16),
             "combine");
     ctx->launches += 1;
   }
@@ -726,7 +727,8 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
     PhaseScope ps(ctx, st, RIALLM_PHASE_COMBINE);
     RL_CUDA(ctx, rl::launch_combine((const float*)(base + L.y_perm), (const int*)(base + L.inv_pos),
                                     (const int*)(base + L.topk_idx), (const float*)(base + L.topk_w), T, k, H,
-                                    nullptr, nullptr, partial, false, false, st, e_begin, e_begin + e_local),
+                                    nullptr, nullptr, partial, false, false, st, e_begin, e_begin + e_local,
+                                    true),
             "combine (partial)");
     ctx->launches += 1;
   }

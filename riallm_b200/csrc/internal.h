@@ -106,12 +106,13 @@ cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int 
                           const int* row_begin = nullptr, const int* row_end = nullptr);
 // out[t] = sum over t's pairs in expert-ascending order of w * y_perm[pos]
 // (+ shared expert), optional residual add, cast to the activation dtype.
-// Pairs whose expert lies outside [e_begin, e_end) are skipped.
+// Pairs whose expert lies outside [e_begin, e_end) are skipped. round_w:
+// the routing weights are rounded to bf16 first (bf16 activations,
+// src/model.rs:800-802).
 cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* topk_idx,
                            const float* topk_w, int T, int k, int H, const float* shared_y,
                            const float* shared_gate, void* out, bool out_bf16, bool add_to_out,
-                           cudaStream_t stream, int e_begin = 0,
-                           int e_end = 1 << 30);
+                           cudaStream_t stream, int e_begin, int e_end, bool round_w);
 
 // Generic CUDA-core grouped GEMM with on-the-fly dequant (float32 path and
 // the shared expert): Y[pos, r] = sum_c X[pos, c] * W[row_base(e) + r, c].

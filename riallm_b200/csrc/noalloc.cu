@@ -33,8 +33,8 @@ static __device__ __align__(256) int g_noalloc_status;
 namespace {
 
 struct DeviceSlot {
-  std::once_flag once;
-  int rc = RIALLM_OK;
+  std::mutex mu;
+  bool ready = false;
   unsigned char* scratch = nullptr;
   int* status = nullptr;
   int num_sms = 0;
@@ -42,41 +42,55 @@ struct DeviceSlot {
 constexpr int kMaxDevices = 64;
 DeviceSlot g_slots[kMaxDevices];
 
-// Per-device set-up, done once with that device current: the device
-// addresses of the scratch array and the status word, and the SM count.
+// Per-device set-up with that device current: the device addresses of the
+// scratch array and the status word, and the SM count. Only a successful
+// set-up is kept; a failed one (for example a first call made inside a
+// stream capture, where the look-up is not allowed) is tried again on the
+// next call.
 int device_setup(int dev, DeviceSlot** out) {
   if (dev < 0 || dev >= kMaxDevices) return RIALLM_ERR_CONFIG;
   DeviceSlot& s = g_slots[dev];
-  std::call_once(s.once, [&] {
+  std::lock_guard<std::mutex> lock(s.mu);
+  if (!s.ready) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) {
-      s.rc = RIALLM_ERR_CUDA;
-      return;
+    void* q = nullptr;
+    int sms = 0;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess ||
+        cudaGetSymbolAddress(&q, g_noalloc_status) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();  // reset the runtime's last-error state; the next call retries
+      return RIALLM_ERR_CUDA;
     }
     s.scratch = static_cast<unsigned char*>(p);
-    if (cudaGetSymbolAddress(&p, g_noalloc_status) != cudaSuccess) {
-      s.rc = RIALLM_ERR_CUDA;
-      return;
-    }
-    s.status = static_cast<int*>(p);
-    if (cudaDeviceGetAttribute(&s.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      s.rc = RIALLM_ERR_CUDA;
-  });
+    s.status = static_cast<int*>(q);
+    s.num_sms = sms;
+    s.ready = true;
+  }
   *out = &s;
-  return s.rc;
+  return RIALLM_OK;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-bool quantized_ok(const riallm_qtensor& t, uint64_t numel) {
-  if (!t.data || t.numel != numel) return false;
-  if (t.qtype == RIALLM_COMPRESSION_FOUR_BIT) return t.block_size == 64 && t.scales && t.zero_points &&
-                                                     aligned16(t.data) && aligned16(t.scales) &&
-                                                     aligned16(t.zero_points);
-  if (t.qtype == RIALLM_COMPRESSION_EIGHT_BIT) return t.block_size == 128 && t.scales && t.zero_points &&
-                                                      aligned16(t.data) && aligned16(t.scales) &&
-                                                      aligned16(t.zero_points);
-  return false;
+// The same checks, in the same order and with the same status codes, as
+// the regular entry point applies to an expert tensor: a missing tensor is
+// RIALLM_ERR_MODEL_LOADING, a wrong element count RIALLM_ERR_CONFIG, an
+// unquantized or malformed one RIALLM_ERR_QUANTIZATION, unaligned buffers
+// RIALLM_ERR_INVALID. need_quantized is false for the router weight, which
+// may also be float32.
+int check_tensor(const riallm_qtensor& t, uint64_t numel, bool need_quantized) {
+  if (!t.data) return RIALLM_ERR_MODEL_LOADING;
+  if (t.numel != numel) return RIALLM_ERR_CONFIG;
+  if (t.qtype == RIALLM_COMPRESSION_NONE) {
+    if (need_quantized) return RIALLM_ERR_QUANTIZATION;
+    return aligned16(t.data) ? RIALLM_OK : RIALLM_ERR_INVALID;
+  }
+  if (t.qtype != RIALLM_COMPRESSION_FOUR_BIT && t.qtype != RIALLM_COMPRESSION_EIGHT_BIT)
+    return RIALLM_ERR_QUANTIZATION;
+  if (t.block_size != (t.qtype == RIALLM_COMPRESSION_FOUR_BIT ? 64 : 128)) return RIALLM_ERR_QUANTIZATION;
+  if (!t.scales || !t.zero_points) return RIALLM_ERR_QUANTIZATION;
+  if (!aligned16(t.data) || !aligned16(t.scales) || !aligned16(t.zero_points)) return RIALLM_ERR_INVALID;
+  return RIALLM_OK;
 }
 
 }  // namespace
@@ -89,12 +103,9 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0 || E > 256 || k > 16 || k > E) return RIALLM_ERR_CONFIG;
   if (H % 256 != 0 || I % 256 != 0) return RIALLM_ERR_CONFIG;
   if (w->shared_gate_proj.data != nullptr) return RIALLM_ERR_CONFIG;  // routed experts only
-  if (w->gate.data == nullptr || w->gate.numel != (uint64_t)E * H) return RIALLM_ERR_MODEL_LOADING;
-  if (w->gate.qtype != RIALLM_COMPRESSION_NONE && !quantized_ok(w->gate, (uint64_t)E * H))
-    return RIALLM_ERR_QUANTIZATION;
-  if (w->gate.qtype == RIALLM_COMPRESSION_NONE && !aligned16(w->gate.data)) return RIALLM_ERR_INVALID;
-  if (!quantized_ok(w->gate_up_proj, (uint64_t)E * 2 * I * H) || !quantized_ok(w->down_proj, (uint64_t)E * H * I))
-    return RIALLM_ERR_QUANTIZATION;
+  if (int rc = check_tensor(w->gate, (uint64_t)E * H, false)) return rc;
+  if (int rc = check_tensor(w->gate_up_proj, (uint64_t)E * 2 * I * H, true)) return rc;
+  if (int rc = check_tensor(w->down_proj, (uint64_t)E * H * I, true)) return rc;
   if (T == 0) return RIALLM_OK;
   if (!x || !out || !aligned16(x) || !aligned16(out)) return RIALLM_ERR_INVALID;
 
@@ -113,15 +124,14 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   char* base = reinterpret_cast<char*>(slot->scratch);
   const int P = T * k;
-  // The status word and the counters in the layout's first kSyncBytes (the
-  // router's completion counter, the expert GEMM's split-tile counters) must
-  // read zero when the call starts. A completed call leaves them at zero, but
-  // one that stopped early (an expired device wait) may not, so both are
-  // cleared on every call. Every other buffer is fully written before it is
-  // read within the call.
-  if (cudaMemsetAsync(slot->status, 0, sizeof(int), st) != cudaSuccess ||
-      cudaMemsetAsync(base + L.sync, 0, rl::kSyncBytes, st) != cudaSuccess)
-    return RIALLM_ERR_CUDA;
+  // The counters in the layout's first kSyncBytes (the router's completion
+  // counter, the expert GEMM's split-tile counters) must read zero when the
+  // call starts. A completed call leaves them at zero, but one that stopped
+  // early (an expired device wait) may not, so they are cleared on every
+  // call. Every other buffer is fully written before it is read within the
+  // call. The status word is not cleared here: it keeps any call's timeout
+  // until riallm_cuda_moe_forward_noalloc_sync reports and clears it.
+  if (cudaMemsetAsync(base + L.sync, 0, rl::kSyncBytes, st) != cudaSuccess) return RIALLM_ERR_CUDA;
   int* topk_idx = reinterpret_cast<int*>(base + L.topk_idx);
   float* topk_w = reinterpret_cast<float*>(base + L.topk_w);
   int* counts = reinterpret_cast<int*>(base + L.counts);
@@ -196,7 +206,23 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   d.pdl = true;  // follows the gate_up GEMM
   if (rl::launch_tc_gemm(d, slot->num_sms, st) != cudaSuccess) return RIALLM_ERR_CUDA;
   if (rl::launch_combine(reinterpret_cast<float*>(base + L.y_perm), inv, topk_idx, topk_w, T, k, H, nullptr,
-                         nullptr, out, true, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st) != cudaSuccess)
+                         nullptr, out, true, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st, 0, 1 << 30,
+                         true) != cudaSuccess)
     return RIALLM_ERR_CUDA;
   return RIALLM_OK;
+}
+
+extern "C" int32_t riallm_cuda_moe_forward_noalloc_sync(void* stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RIALLM_ERR_CUDA;
+  DeviceSlot* slot = nullptr;
+  if (int rc = device_setup(dev, &slot)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(st) != cudaSuccess) return RIALLM_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, slot->status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return RIALLM_ERR_CUDA;
+  if (v == 0) return RIALLM_OK;
+  if (cudaMemsetAsync(slot->status, 0, sizeof(int), st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess)
+    return RIALLM_ERR_CUDA;
+  return v;
 }

@@ -357,7 +357,7 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
                                const int* __restrict__ topk_idx, const float* __restrict__ topk_w,
                                int k, int H, const float* __restrict__ shared_y,
                                const float* __restrict__ shared_gate, void* out, int out_bf16,
-                               int add_to_out, int e_begin, int e_end) {
+                               int add_to_out, int e_begin, int e_end, int round_w) {
   pdl_wait();  // y_perm comes from the down GEMM
   pdl_launch_dependents();
   const int t = blockIdx.x;
@@ -385,7 +385,10 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
       // Expert-parallel partial sums keep only this rank's experts.
       if (exp_id[j] < e_begin || exp_id[j] >= e_end) continue;
       const int pos = inv_pos[(uint64_t)t * k + j];
-      const float w = topk_w[(uint64_t)t * k + j];
+      // src/model.rs:800-802: the weight is cast to the activation dtype
+      // (bf16 rounding for bf16 activations) before it scales y.
+      const float w0 = topk_w[(uint64_t)t * k + j];
+      const float w = round_w ? __bfloat162float(__float2bfloat16_rn(w0)) : w0;
       const float4 y = *reinterpret_cast<const float4*>(y_perm + (uint64_t)pos * H + h);
       a0 = __fadd_rn(a0, __fmul_rn(y.x, w));
       a1 = __fadd_rn(a1, __fmul_rn(y.y, w));
@@ -428,12 +431,13 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
 cudaError_t launch_combine(const float* y_perm, const int* inv_pos, const int* topk_idx,
                            const float* topk_w, int T, int k, int H, const float* shared_y,
                            const float* shared_gate, void* out, bool out_bf16, bool add_to_out,
-                           cudaStream_t stream, int e_begin, int e_end) {
+                           cudaStream_t stream, int e_begin, int e_end, bool round_w) {
   if (T == 0) return cudaSuccess;
   const int threads = H >= 1024 ? 256 : 128;
   const dim3 grid(T, (H + threads * 4 - 1) / (threads * 4));
   return launch_pdl(combine_kernel, grid, dim3(threads), 0, stream, y_perm, inv_pos, topk_idx, topk_w, k, H,
-                    shared_y, shared_gate, out, out_bf16 ? 1 : 0, add_to_out ? 1 : 0, e_begin, e_end);
+                    shared_y, shared_gate, out, out_bf16 ? 1 : 0, add_to_out ? 1 : 0, e_begin, e_end,
+                    round_w ? 1 : 0);
 }
 
 // ------------------------------------------------- CUDA-core grouped GEMM

@@ -12,6 +12,12 @@
 // release(layer) records the compute stream's progress for the slot's next
 // copy. No host synchronisation is involved, so copies of layers i+1 ..
 // i+depth-1 overlap the compute of layer i.
+//
+// Copy timing uses a fixed ring of 4 x depth event pairs created with the
+// streamer: a pair's elapsed time is added to the total when the pair is
+// reused (waiting for that old copy if the host has run that far ahead of
+// the copy stream) or when stats() is read, so a long streamed run keeps a
+// constant number of events.
 #include <vector>
 
 #include "internal.h"
@@ -26,7 +32,8 @@ struct riallm_streamer {
   std::vector<cudaEvent_t> ready, freed;
   std::vector<int> layer;   // layer held by each slot, -1 when none
   std::vector<int> state;   // 0 empty, 1 copy issued, 2 acquired, 3 released
-  std::vector<cudaEvent_t> t_start, t_stop;  // per issued copy, read by stats
+  std::vector<cudaEvent_t> t_start, t_stop;  // timing ring: one pair per copy in flight
+  std::vector<char> t_pending;                // pair i timed a copy not yet added to copy_ms
   uint64_t bytes = 0, copies = 0;
   double copy_ms = 0.0;
 };
@@ -44,6 +51,17 @@ int fail(riallm_ctx* ctx, int code, const std::string& msg) {
     if (e_ != cudaSuccess)                                                            \
       return fail((s)->ctx, RIALLM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e_)); \
   } while (0)
+
+// Adds the copy timed by ring pair i to the total (waiting for it to end).
+int fold_timing(riallm_streamer* s, size_t i) {
+  if (!s->t_pending[i]) return RIALLM_OK;
+  ST_CUDA(s, cudaEventSynchronize(s->t_stop[i]), "cudaEventSynchronize");
+  float ms = 0.f;
+  ST_CUDA(s, cudaEventElapsedTime(&ms, s->t_start[i], s->t_stop[i]), "cudaEventElapsedTime");
+  s->copy_ms += ms;
+  s->t_pending[i] = 0;
+  return RIALLM_OK;
+}
 
 void destroy(riallm_streamer* s) {
   if (!s) return;
@@ -99,6 +117,16 @@ int32_t riallm_cuda_streamer_create(riallm_ctx* ctx, int32_t depth, uint64_t slo
     s->ready.push_back(a);
     s->freed.push_back(b);
   }
+  for (int i = 0; rc == RIALLM_OK && i < 4 * depth; ++i) {
+    cudaEvent_t a, b;
+    if (cudaEventCreate(&a) != cudaSuccess || cudaEventCreate(&b) != cudaSuccess) {
+      rc = fail(ctx, RIALLM_ERR_CUDA, "streamer: cudaEventCreate");
+      break;
+    }
+    s->t_start.push_back(a);
+    s->t_stop.push_back(b);
+    s->t_pending.push_back(0);
+  }
   if (rc != RIALLM_OK) {
     destroy(s);
     return rc;
@@ -125,16 +153,15 @@ int32_t riallm_cuda_streamer_prefetch(riallm_streamer* s, int32_t layer, const v
   ST_CUDA(s, cudaSetDevice(s->ctx->device), "cudaSetDevice");
   // The slot's previous layer must be done with before it is overwritten.
   if (s->state[slot] == 3) ST_CUDA(s, cudaStreamWaitEvent(s->copy, s->freed[slot], 0), "wait slot release");
-  cudaEvent_t a, b;
-  ST_CUDA(s, cudaEventCreate(&a), "cudaEventCreate");
-  ST_CUDA(s, cudaEventCreate(&b), "cudaEventCreate");
-  s->t_start.push_back(a);
-  s->t_stop.push_back(b);
+  const size_t ti = (size_t)(s->copies % s->t_start.size());
+  if (int rc = fold_timing(s, ti)) return rc;
+  cudaEvent_t a = s->t_start[ti], b = s->t_stop[ti];
   ST_CUDA(s, cudaEventRecord(a, s->copy), "cudaEventRecord");
   ST_CUDA(s, cudaMemcpyAsync(s->dev + (uint64_t)slot * s->slot_bytes, host_src, bytes, cudaMemcpyHostToDevice,
                              s->copy),
           "streamer H2D");
   ST_CUDA(s, cudaEventRecord(b, s->copy), "cudaEventRecord");
+  s->t_pending[ti] = 1;
   ST_CUDA(s, cudaEventRecord(s->ready[slot], s->copy), "cudaEventRecord");
   s->layer[slot] = layer;
   s->state[slot] = 1;
@@ -170,15 +197,8 @@ int32_t riallm_cuda_streamer_stats(riallm_streamer* s, uint64_t* bytes, uint64_t
   if (!s) return RIALLM_ERR_INVALID;
   ST_CUDA(s, cudaSetDevice(s->ctx->device), "cudaSetDevice");
   ST_CUDA(s, cudaStreamSynchronize(s->copy), "cudaStreamSynchronize");
-  for (size_t i = 0; i < s->t_start.size(); ++i) {
-    float ms = 0.f;
-    ST_CUDA(s, cudaEventElapsedTime(&ms, s->t_start[i], s->t_stop[i]), "cudaEventElapsedTime");
-    s->copy_ms += ms;
-    cudaEventDestroy(s->t_start[i]);
-    cudaEventDestroy(s->t_stop[i]);
-  }
-  s->t_start.clear();
-  s->t_stop.clear();
+  for (size_t i = 0; i < s->t_start.size(); ++i)
+    if (int rc = fold_timing(s, i)) return rc;
   if (bytes) *bytes = s->bytes;
   if (copies) *copies = s->copies;
   if (copy_ms) *copy_ms = s->copy_ms;

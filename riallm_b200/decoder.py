@@ -63,12 +63,13 @@ class DecoderConfig:
                    vocab=32000, experts=8, top_k=2, intermediate=14336)
 
 
-def _layer_weights(cfg: DecoderConfig, l: int, n, device) -> Dict[str, torch.Tensor]:
+def _layer_weights(cfg: DecoderConfig, l: int, n, device, alt_norm: bool = True) -> Dict[str, torch.Tensor]:
     H, I, E = cfg.hidden, cfg.intermediate, cfg.experts
     kvd = cfg.kv_heads * cfg.head_dim
     p = f"model.layers.{l}."
     alt = torch.ones(H, device=device)
-    alt[1::2] = -1.0
+    if alt_norm:
+        alt[1::2] = -1.0
     return {p + "input_layernorm.weight": torch.ones(H, device=device),
             p + "self_attn.q_proj.weight": n(cfg.heads * cfg.head_dim, H),
             p + "self_attn.k_proj.weight": n(kvd, H),
@@ -89,14 +90,16 @@ def _normal(device, seed, expert_std):
 
 
 def synthetic_weights(cfg: DecoderConfig, seed: int = 0, device: str = "cuda",
-                      expert_std: float = 4e-4) -> Dict[str, torch.Tensor]:
+                      expert_std: float = 4e-4, alt_norm: bool = True) -> Dict[str, torch.Tensor]:
     """float32 weights from a seeded torch generator on `device` in a fixed
     order: N(0, 0.02), the expert tensors N(0, expert_std); RMSNorm weights
-    are 1.0 except the one in front of the MoE block, which alternates +1/-1."""
+    are 1.0 except the one in front of the MoE block, which alternates +1/-1
+    when alt_norm is set. expert_std=0.02 with alt_norm=False is the tiny
+    configuration exactly as specified (every weight N(0, 0.02), unit norms)."""
     n = _normal(device, seed, expert_std)
     w = {"model.embed_tokens.weight": n(cfg.vocab, cfg.hidden)}
     for l in range(cfg.layers):
-        w.update(_layer_weights(cfg, l, n, device))
+        w.update(_layer_weights(cfg, l, n, device, alt_norm))
     w["model.norm.weight"] = torch.ones(cfg.hidden, device=device)
     w["lm_head.weight"] = n(cfg.vocab, cfg.hidden)
     return w
