@@ -78,6 +78,8 @@ CASES = [
     (17, 256, 512, 4, 1, 1, True),
     (64, 512, 512, 8, 2, 1, True),
     (130, 256, 256, 2, 2, 1, True),    # 130 pairs per expert: two N tiles (128 + 16)
+    (60, 256, 512, 2, 1, 1, True),     # decode-sized, > 32 pairs on an expert: scale/zero decoded into A
+    (2, 4096, 1024, 8, 2, 1, True),    # <= 16 pairs per tile: codes-only A, 16-column ring layout
     (300, 256, 256, 4, 2, 2, True),    # N tile widths 128/64/32/16 across experts
     (9, 256, 256, 8, 2, 1, False),
     (40, 512, 256, 8, 4, 2, False),
