@@ -30,7 +30,7 @@ __all__ = [
     "CompressionType", "DeviceSpec", "ModelOptions", "QuantizedTensor", "quantize_tensor",
     "compress_layer_state_dict", "dequantize_layer_state_dict", "apply_moe", "route", "Context",
     "RiallmError", "ModelLoadingError", "MemoryError_", "ConfigError", "QuantizationError",
-    "CudaError", "TimeoutError_", "lib",
+    "CudaError", "TimeoutError_", "lib", "AutoModel", "ModelConfig",
 ]
 
 
@@ -513,3 +513,12 @@ def route(gate: TensorLike, hidden: torch.Tensor, num_experts_per_tok: int, num_
                                           counts.data_ptr(), offsets.data_ptr(), perm.data_ptr(),
                                           _stream_ptr(flat)))
     return idx, tw, counts, offsets, perm
+
+
+def __getattr__(name: str):
+    """AutoModel / ModelConfig (src/auto_model.rs, src/config.rs) live in
+    riallm_b200.auto_model and are loaded on first use."""
+    if name in ("AutoModel", "ModelConfig"):
+        from . import auto_model
+        return getattr(auto_model, name)
+    raise AttributeError(f"module 'riallm_b200' has no attribute {name!r}")

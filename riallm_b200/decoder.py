@@ -173,7 +173,13 @@ class Decoder:
     KV cache of `max_seq` positions per sequence."""
 
     def __init__(self, cfg: DecoderConfig, qweights: Dict[str, object], max_batch: int = 1,
-                 max_seq: int = 2048, device: int = 0):
+                 max_seq: int = 2048, device: int = 0, streamer=None):
+        """streamer: a LayerStreamer over the layers' MoE tensors (router
+        gate and experts, one PackedLayer per layer, in layer order); they
+        are then not taken from qweights but copied from pinned host memory
+        into the streamer's device slots ahead of each layer on every forward
+        (ModelOptions.prefetch_layers). Such a decoder runs its decode steps
+        eagerly (the copies are host-driven, so there is no decode graph)."""
         c = self.cfg = cfg
         if c.heads % c.kv_heads or c.heads // c.kv_heads not in (1, 2, 4, 8) or c.head_dim not in (64, 128):
             raise ConfigError("need heads / kv_heads in {1, 2, 4, 8} and head_dim 64 or 128")
@@ -195,9 +201,13 @@ class Decoder:
                 "post_norm": qweights[p + "post_attention_layernorm.weight"].float().contiguous(),
                 "wqkv": torch.cat([_bf16(qweights[p + f"self_attn.{n}_proj.weight"]) for n in "qkv"], 0),
                 "wo": _bf16(qweights[p + "self_attn.o_proj.weight"]),
-                "moe": {k: qweights[p + k] for k in ("mlp.gate.weight", "mlp.experts.gate_up_proj",
-                                                     "mlp.experts.down_proj")},
+                "moe": None if streamer is not None else {
+                    k: qweights[p + k] for k in ("mlp.gate.weight", "mlp.experts.gate_up_proj",
+                                                 "mlp.experts.down_proj")},
             })
+        self.streamer = streamer
+        if streamer is not None and len(streamer.layers) != c.layers:
+            raise ConfigError(f"streamer holds {len(streamer.layers)} layers, the model {c.layers}")
         self.max_batch, self.max_seq = max_batch, max_seq
         shape = (max_batch, c.kv_heads, max_seq, c.head_dim)
         self.k_cache = [torch.zeros(shape, dtype=torch.bfloat16, device=self.dev) for _ in range(c.layers)]
@@ -247,6 +257,10 @@ class Decoder:
         q = torch.empty(B * T, nh * d, dtype=torch.bfloat16, device=self.dev)
         att = torch.empty_like(q)
         L = lib()
+        st = self.streamer
+        if st is not None:
+            for i in range(min(st.depth, c.layers)):
+                st.prefetch(i)
         for i, layer in enumerate(self.layers):
             self._norm(h, layer["in_norm"], n)
             qkv = self._linear(n, layer["wqkv"])
@@ -259,10 +273,14 @@ class Decoder:
                                                    att.data_ptr(), self._st()))
             o = self._linear(att, layer["wo"])
             self._norm(h, layer["post_norm"], n, delta=o)         # h += o; n = norm(h)
+            moe = layer["moe"] if st is None else st.acquire(i)
             if experts_used is not None:
-                counts = route(layer["moe"]["mlp.gate.weight"], n, c.top_k, c.experts, ctx=moe_ctx)[2]
+                counts = route(moe["mlp.gate.weight"], n, c.top_k, c.experts, ctx=moe_ctx)[2]
                 experts_used.append(int((counts > 0).sum().item()))
-            apply_moe(layer["moe"], n, c.top_k, c.experts, out=h, add_to_out=True, ctx=moe_ctx)
+            apply_moe(moe, n, c.top_k, c.experts, out=h, add_to_out=True, ctx=moe_ctx)
+            if st is not None:
+                st.release(i)
+                st.prefetch(i + st.depth)
         self.pos[:B].add_(T)
         last = h.view(B, T, -1)[:, -1].contiguous()
         nl = torch.empty_like(last)
@@ -323,7 +341,7 @@ class Decoder:
         logits = self.forward(prompt)
         tok = torch.argmax(logits, -1)
         toks, kept = [tok], ([logits] if keep_logits else [])
-        step = self._decode_graph(B) if use_graph and new_tokens > 1 else None
+        step = self._decode_graph(B) if use_graph and new_tokens > 1 and self.streamer is None else None
         for _ in range(new_tokens - 1):
             self._advance(B, 1)
             if step is not None:
@@ -350,6 +368,11 @@ class Decoder:
         greedy ids of each step are computed and dropped. Measures the decode
         step with a chosen continuation."""
         S, B = ids.shape[0], ids.shape[1]
+        if self.streamer is not None:
+            for i in range(S):
+                self._advance(B, 1)
+                self._forward(ids[i])
+            return
         g, buf, _, _ = self._decode_graph(B)
         for i in range(S):
             self._advance(B, 1)

@@ -21,12 +21,64 @@ a CPU implementation to check the orchestration with gloo ranks.
 """
 from __future__ import annotations
 
+import datetime
 from typing import Callable, Mapping, Optional
 
 import torch
 import torch.distributed as dist
 
-from . import ConfigError, TensorLike, apply_moe_ep_partial
+from . import ConfigError, RiallmError, TensorLike, apply_moe_ep_partial
+
+
+class RankFailureError(RiallmError):
+    """A peer rank stopped taking part in the expert-parallel steps (it
+    exited, crashed or hangs). Raised on the surviving ranks on the host,
+    before any of the failed step's collectives or kernels are launched when
+    a PeerWatch is in use, or when a collective of the step fails or times
+    out. `ranks` lists the peers known to be missing (empty if unknown)."""
+
+    def __init__(self, msg: str, ranks=()):
+        super().__init__(msg)
+        self.ranks = tuple(ranks)
+
+
+class PeerWatch:
+    """Host-side liveness check between expert-parallel steps.
+
+    Before step n each rank posts the key `<prefix>/<rank>/<n>` to the
+    process group's key-value store and waits, at most `timeout_s` seconds,
+    for every peer's key of the same step. A rank that has left (between
+    steps, with none of its kernels or collectives in flight) therefore
+    stops the others on the host, with the missing ranks named, instead of
+    leaving them blocked inside a collective. Each rank deletes its own key
+    of step n - 2, so the store stays small."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 5.0, prefix: str = "riallm/ep/step"):
+        self.store, self.rank, self.world = store, int(rank), int(world)
+        self.timeout = datetime.timedelta(seconds=float(timeout_s))
+        self.prefix = prefix
+        self.n = 0
+
+    def _key(self, r: int, n: int) -> str:
+        return f"{self.prefix}/{r}/{n}"
+
+    def step(self) -> None:
+        n = self.n
+        self.store.set(self._key(self.rank, n), "1")
+        peers = [self._key(r, n) for r in range(self.world) if r != self.rank]
+        try:
+            if peers:
+                self.store.wait(peers, self.timeout)
+        except Exception as exc:  # the store's timeout error type differs by store and version
+            missing = [r for r in range(self.world) if r != self.rank and not self.store.check([self._key(r, n)])]
+            raise RankFailureError(f"expert-parallel step {n}: rank(s) {missing} did not arrive within "
+                                   f"{self.timeout.total_seconds():g} s ({exc})", missing) from None
+        if n >= 2:
+            try:
+                self.store.delete_key(self._key(self.rank, n - 2))
+            except Exception:
+                pass
+        self.n += 1
 
 PartialFn = Callable[[torch.Tensor, int, int], torch.Tensor]
 
@@ -50,7 +102,8 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, tensors: Mapping[str, TensorLike], num_experts: int, top_k: int,
-                 group: Optional[dist.ProcessGroup] = None, ops: Optional[PartialFn] = None):
+                 group: Optional[dist.ProcessGroup] = None, ops: Optional[PartialFn] = None,
+                 watch: Optional[PeerWatch] = None):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -61,11 +114,24 @@ class ExpertParallelMoE:
         self.ops = ops or self._gpu_partial
         # gloo has no reduce-scatter: it all-reduces and keeps its own slice.
         self.backend = dist.get_backend(group)
+        self.watch = watch
 
     def _gpu_partial(self, x_all: torch.Tensor, e_begin: int, e_local: int) -> torch.Tensor:
         return apply_moe_ep_partial(self.tensors, x_all, self.k, self.E, e_begin, e_local)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.watch is not None:
+            self.watch.step()
+        try:
+            return self._forward(x)
+        except RiallmError:
+            raise
+        except RuntimeError as exc:
+            # A collective that failed or timed out (a peer left during the
+            # step, or the process group's timeout expired).
+            raise RankFailureError(f"expert-parallel collective failed: {exc}") from exc
+
+    def _forward(self, x: torch.Tensor) -> torch.Tensor:
         T, H = x.shape
         W = self.world
         x = x.contiguous()

@@ -35,18 +35,38 @@ _DT = {"F32": torch.float32, "F16": torch.float16, "BF16": torch.bfloat16, "I64"
 _DT_INV = {v: k for k, v in _DT.items()}
 
 
-def read_safetensors(path: str, names: Optional[Iterable[str]] = None) -> Dict[str, torch.Tensor]:
-    """Tensors of a safetensors file (all, or those named), on the CPU."""
-    with open(path, "rb") as f:
-        (n,) = struct.unpack("<Q", f.read(8))
+def _read_header(f, path: str):
+    """The JSON header of an open safetensors file and the data offset.
+    A file cut short (or not a safetensors file) is a ModelLoadingError."""
+    size = os.fstat(f.fileno()).st_size
+    raw = f.read(8)
+    if len(raw) < 8:
+        raise ModelLoadingError(f"truncated safetensors file (no header length): {path}")
+    (n,) = struct.unpack("<Q", raw)
+    if n > size - 8:
+        raise ModelLoadingError(f"truncated safetensors file (header of {n} bytes, file of {size}): {path}")
+    try:
         header = json.loads(f.read(n))
-        base = 8 + n
+    except (ValueError, UnicodeDecodeError) as exc:
+        raise ModelLoadingError(f"corrupt safetensors header in {path}: {exc}") from None
+    return header, 8 + n, size
+
+
+def read_safetensors(path: str, names: Optional[Iterable[str]] = None) -> Dict[str, torch.Tensor]:
+    """Tensors of a safetensors file (all, or those named), on the CPU.
+    Raises ModelLoadingError when the file is shorter than its header says
+    (a shard cut off mid-write or mid-copy)."""
+    with open(path, "rb") as f:
+        header, base, size = _read_header(f, path)
         want = set(names) if names is not None else None
         out = {}
         for name, info in header.items():
             if name == "__metadata__" or (want is not None and name not in want):
                 continue
             b, e = info["data_offsets"]
+            if not (0 <= b <= e) or base + e > size:
+                raise ModelLoadingError(f"truncated safetensors file: tensor {name} needs bytes "
+                                        f"[{base + b}, {base + e}) of a {size}-byte file {path}")
             f.seek(base + b)
             buf = bytearray(f.read(e - b))
             dt = _DT[info["dtype"]]
@@ -57,8 +77,7 @@ def read_safetensors(path: str, names: Optional[Iterable[str]] = None) -> Dict[s
 
 def read_safetensors_metadata(path: str) -> Dict[str, str]:
     with open(path, "rb") as f:
-        (n,) = struct.unpack("<Q", f.read(8))
-        return json.loads(f.read(n)).get("__metadata__", {})
+        return _read_header(f, path)[0].get("__metadata__", {})
 
 
 def write_safetensors(path: str, tensors: Mapping[str, torch.Tensor], metadata: Optional[Dict[str, str]] = None):
@@ -102,8 +121,7 @@ class CheckpointIndex:
                 if fn.endswith(".safetensors"):
                     p = os.path.join(directory, fn)
                     with open(p, "rb") as f:
-                        (n,) = struct.unpack("<Q", f.read(8))
-                        for name in json.loads(f.read(n)):
+                        for name in _read_header(f, p)[0]:
                             if name != "__metadata__":
                                 self.where[name] = p
 
@@ -231,8 +249,11 @@ def load_quant_state(path: str, honor_qtype: bool = True) -> Dict[str, Quantized
     block_size defaults to 128 as there."""
     if not os.path.exists(path):
         return {}
-    with open(path) as f:
-        ser = json.load(f)
+    try:
+        with open(path) as f:
+            ser = json.load(f)
+    except ValueError as exc:
+        raise ModelLoadingError(f"corrupt quant-state file {path}: {exc}") from None
     out = {}
     for name, d in ser.items():
         qt = CompressionType.EightBit

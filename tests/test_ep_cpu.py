@@ -93,3 +93,54 @@ def test_expert_range_and_slice_rules():
     assert expert_range(128, 7, 8) == (112, 16)
     with pytest.raises(ConfigError):
         expert_range(8, 0, 3)
+
+
+def _leaver(rank, world, port, result_dir, use_watch):
+    """Both ranks take one step; rank 1 then leaves (between steps, nothing
+    in flight). Rank 0's next step must raise RankFailureError on the host:
+    from the PeerWatch before any collective, or from the short process-group
+    timeout of the collective itself."""
+    import datetime
+    import sys
+    import time
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from riallm_b200.ep import ExpertParallelMoE, PeerWatch, RankFailureError
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0, timeout=datetime.timedelta(seconds=20))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    watch = PeerWatch(store, rank, world, timeout_s=2.0) if use_watch else None
+
+    def ops(xt, e_begin, e_local):
+        return torch.zeros(xt.shape, dtype=torch.float32)
+
+    blk = ExpertParallelMoE({}, E, K, ops=ops, watch=watch)
+    x = torch.zeros(T_LOCAL, H, dtype=torch.bfloat16)
+    blk(x)
+    if rank == 1:
+        # Leave without tearing down the group: a process that died.
+        os._exit(0)
+    t0 = time.time()
+    try:
+        blk(x)
+        msg = "no error"
+    except RankFailureError as exc:
+        msg = f"RankFailureError ranks={list(exc.ranks)} after {time.time() - t0:.1f}s"
+    with open(os.path.join(result_dir, "rank0.txt"), "w") as f:
+        f.write(msg)
+    os._exit(0)
+
+
+@pytest.mark.parametrize("use_watch", [True, False])
+def test_rank_that_leaves_is_reported(tmp_path, use_watch):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_leaver, args=(r, 2, port, str(tmp_path), use_watch)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(60)
+        assert not p.is_alive()
+    msg = open(tmp_path / "rank0.txt").read()
+    assert msg.startswith("RankFailureError"), msg
+    if use_watch:
+        assert "ranks=[1]" in msg, msg

@@ -115,3 +115,38 @@ def test_quant_state_json_matches_reference_format(tmp_path):
     # The reference's loader ignores the stored qtype (always EightBit).
     assert L.load_quant_state(p, honor_qtype=False)["w"].qtype == CompressionType.EightBit
     assert L.load_quant_state(str(tmp_path / "missing.json")) == {}
+
+
+def test_truncated_files_are_loading_errors(tmp_path):
+    """A shard or quant-state file cut short (an interrupted write or copy)
+    raises ModelLoadingError naming the file, never a bare decode error."""
+    E, H, I = 4, 256, 128
+    _fake_mixtral(tmp_path / "ckpt", E, H, I, layers=1)
+    shard = tmp_path / "ckpt" / "model-00000.safetensors"
+    full = shard.read_bytes()
+    for cut in (4, 12, len(full) // 2, len(full) - 1):
+        shard.write_bytes(full[:cut])
+        with pytest.raises(ModelLoadingError, match="safetensors"):
+            L.read_safetensors(str(shard))
+    shard.write_bytes(full[:len(full) - 1])
+    idx = L.CheckpointIndex(str(tmp_path / "ckpt"))
+    with pytest.raises(ModelLoadingError, match="truncated"):
+        L.mixtral_moe_layer(idx, 0, E)
+    # A cached quantized shard cut short is refused too.
+    shard.write_bytes(full)
+    cache = L.QuantizedShardCache(str(tmp_path / "cache"), CompressionType.FourBit, quantize=_oracle_quantize)
+    cache.layer(0, lambda: L.mixtral_moe_layer(L.CheckpointIndex(str(tmp_path / "ckpt")), 0, E))
+    cp = cache.path(0)
+    data = open(cp, "rb").read()
+    with open(cp, "wb") as f:
+        f.write(data[:-100])
+    with pytest.raises(ModelLoadingError, match="truncated"):
+        cache.load(0)
+    q = _oracle_quantize(torch.randn(64 * 70), CompressionType.FourBit)
+    p = str(tmp_path / "state.json")
+    L.save_quant_state({"w": q}, p)
+    text = open(p).read()
+    with open(p, "w") as f:
+        f.write(text[:len(text) // 2])
+    with pytest.raises(ModelLoadingError, match="quant-state"):
+        L.load_quant_state(p)
