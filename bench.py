@@ -461,6 +461,7 @@ def run_ours(args, rank, world, local):
     decode = None if args.no_decode else decode_measure(rb, torch, device, decode_batches(args),
                                                         new_tokens=args.decode_new)
     fine = None if args.no_sweep else fine_grained_measure(rb, torch, device)
+    quant = None if args.no_sweep else quant_measure(rb, torch, device, d, hbm_peak, peak_src)
 
     if rank == 0:
         line = {
@@ -474,7 +475,7 @@ def run_ours(args, rank, world, local):
             "gpu_launches_note": f"{launches_per_step} kernels per step (router, gather, expert gate_up and down GEMMs, combine) replayed from one CUDA graph",
             "captured_launches": per_step_launches,
             "clocks": clk.summary(), "sweep": sweep, "streaming": streaming, "streaming_8x22b": streaming_8x22b,
-            "decode": decode, "fine_grained": fine,
+            "decode": decode, "fine_grained": fine, "quant": quant,
         }
         print(json.dumps(line), flush=True)
     del g
@@ -772,6 +773,54 @@ def zipf_bias(torch, n, s=1.1, seed=4):
     ranks = torch.randperm(n, generator=g).double() + 1.0
     w = ranks ** -s
     return torch.log(w / w.sum()).float()
+
+
+def quant_measure(rb, torch, device, d, hbm_peak, peak_src, reps=5):
+    """The standalone block dequantizer and quantizer (src/quantization.rs:
+    45-245) on the Mixtral-8x7B layer's gate_up_proj (8 x 28672 x 4096 =
+    939,524,096 weights): HBM GB/s = algorithmic bytes (codes + float32
+    scales and zero points read, values written; or float32 read and codes,
+    scales, zero points written) / CUDA-event time on the launching stream,
+    best of `reps` launches after one warm-up, against the measured copy
+    peak. Inputs and outputs are larger than L2."""
+    gu = d["mlp.experts.gate_up_proj"]
+    n = gu.numel
+    out = {"tensor": "mixtral8x7b gate_up_proj [8, 28672, 4096]", "elements": n,
+           "peak": hbm_peak, "peak_source": peak_src, "runs": []}
+
+    def best(fn):
+        fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return min(ts)
+
+    def entry(name, nbytes, ms):
+        gbs = nbytes / (ms / 1000.0) / 1e9
+        out["runs"].append({"op": name, "bytes": int(nbytes), "ms": round(ms, 4), "gbs": round(gbs, 1),
+                            "frac": round(gbs / hbm_peak, 4)})
+
+    code_b = gu.data.numel() + 8 * gu.scales.numel()
+    for dt, esz in ((torch.bfloat16, 2), (torch.float32, 4)):
+        ms = best(lambda: gu.dequantize(dt))
+        entry(f"dequantize NF4 -> {str(dt).split('.')[-1]}", code_b + esz * n, ms)
+    src = gu.dequantize(torch.float32)  # any float32 values of this size
+    for c, name in ((rb.CompressionType.EightBit, "8-bit"), (rb.CompressionType.FourBit, "NF4")):
+        ms = best(lambda: rb.quantize_tensor(src, c))
+        q = rb.quantize_tensor(src, c)
+        entry(f"quantize float32 -> {name}", 4 * n + q.data.numel() + 8 * q.scales.numel(), ms)
+        if c == rb.CompressionType.EightBit:
+            ms = best(lambda: q.dequantize(torch.bfloat16))
+            entry("dequantize 8-bit -> bfloat16", q.data.numel() + 8 * q.scales.numel() + 2 * n, ms)
+        del q
+    del src
+    return out
 
 
 def fine_grained_measure(rb, torch, device, steps=20):

@@ -112,7 +112,27 @@ int32_t riallm_cuda_memcpy_h2d_async(riallm_ctx* ctx, void* dst, const void* src
                                      uint64_t bytes, void* stream);
 int32_t riallm_cuda_memcpy_d2h_async(riallm_ctx* ctx, void* dst, const void* src,
                                      uint64_t bytes, void* stream);
+/* Waits for `stream`; returns RIALLM_ERR_TIMEOUT (and clears the record and
+ * the scratch arena's call counters, so the context stays usable) when a
+ * kernel of this context aborted because a bounded device-side wait
+ * expired. riallm reports failures only as Result<_, RiallmError>
+ * (src/error.rs:8-47); it has no device-side failure of this kind. */
 int32_t riallm_cuda_stream_synchronize(riallm_ctx* ctx, void* stream);
+
+/* No counterpart in the reference. Bound, in ns, of a kernel's wait for
+ * work that other CTAs of the same launch publish (the expert GEMM's
+ * split-tile owner waiting for partial sums). 0 restores the default of 1 s;
+ * other values must be >= 1000. Waits inside a CTA (its own pipeline) keep
+ * the 1 s bound. */
+int32_t riallm_cuda_ctx_set_wait_limit(riallm_ctx* ctx, uint64_t wait_ns);
+
+/* No counterpart in the reference; a test hook for the timeout path. In the
+ * next riallm_cuda_moe_forward call of this context, every expert-GEMM tile
+ * that is split across CTAs is finished by a CTA that waits for a partial-sum
+ * count no CTA reaches, so its bounded wait expires: that CTA stops, the
+ * call's output is undefined, and riallm_cuda_stream_synchronize returns
+ * RIALLM_ERR_TIMEOUT. Nothing faults or hangs; later calls are unaffected. */
+int32_t riallm_cuda_ctx_expire_next_wait(riallm_ctx* ctx);
 int32_t riallm_cuda_memory_stats(riallm_ctx* ctx, uint64_t* free_bytes,
                                  uint64_t* total_bytes);
 

@@ -99,6 +99,8 @@ SIGNATURES = {
     "riallm_cuda_memcpy_h2d_async": (_i32, [_vp, _vp, _vp, _u64, _vp]),
     "riallm_cuda_memcpy_d2h_async": (_i32, [_vp, _vp, _vp, _u64, _vp]),
     "riallm_cuda_stream_synchronize": (_i32, [_vp, _vp]),
+    "riallm_cuda_ctx_set_wait_limit": (_i32, [_vp, _u64]),
+    "riallm_cuda_ctx_expire_next_wait": (_i32, [_vp]),
     "riallm_cuda_memory_stats": (_i32, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
     "riallm_quant_num_blocks": (_u64, [_i32, _u64]),
     "riallm_quant_data_bytes": (_u64, [_i32, _u64]),
@@ -242,6 +244,15 @@ class Context:
     def synchronize(self, stream: Optional[torch.cuda.Stream] = None) -> None:
         s = (stream or torch.cuda.current_stream(self.device)).cuda_stream
         self.check(lib().riallm_cuda_stream_synchronize(self.ptr, s))
+
+    def set_wait_limit(self, wait_ns: int) -> None:
+        """Bound of a kernel's wait for other CTAs' published work (0: 1 s)."""
+        self.check(lib().riallm_cuda_ctx_set_wait_limit(self.ptr, int(wait_ns)))
+
+    def expire_next_wait(self) -> None:
+        """Test hook: the next MoE call's split-tile owners wait for a count
+        that is never reached; synchronize() then raises TimeoutError_."""
+        self.check(lib().riallm_cuda_ctx_expire_next_wait(self.ptr))
 
     def reserve(self, T: int, H: int, I: int, E: int, k: int, dtype: torch.dtype) -> None:
         self.check(lib().riallm_cuda_moe_reserve(self.ptr, T, H, I, E, k, _act_dtype(dtype)))

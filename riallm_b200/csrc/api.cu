@@ -530,6 +530,13 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     d.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
     d.pdl = true;  // follows the gate_up GEMM
     g.next = &d;  // gate_up prefetches the down launch's first weight stages
+    g.flag_wait_ns = d.flag_wait_ns = ctx->flag_wait_ns;
+    if (ctx->expire_next_wait) {
+      // Test hook: both launches' split-tile owners wait for a partial-sum
+      // count no CTA reaches, so their bounded waits expire.
+      g.flag_extra = d.flag_extra = 1 << 20;
+      ctx->expire_next_wait = false;
+    }
     {
       PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
       RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
@@ -699,6 +706,7 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
   g.sk_ws = L.sk_ws ? (float*)(base + L.sk_ws) : nullptr;
   g.sk_flags = (int*)(base + L.sync + rl::kSkFlagsOffset);
   g.pdl = true;  // follows the gather
+  g.flag_wait_ns = ctx->flag_wait_ns;
   {
     PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
     RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
@@ -733,6 +741,20 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
     ctx->launches += 1;
   }
   if (ctx->profiling) ctx->profiled_calls += 1;
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_ctx_set_wait_limit(riallm_ctx* ctx, uint64_t wait_ns) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  if (wait_ns != 0 && wait_ns < 1000)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "wait limit must be 0 (default) or at least 1000 ns");
+  ctx->flag_wait_ns = wait_ns;
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_ctx_expire_next_wait(riallm_ctx* ctx) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  ctx->expire_next_wait = true;
   return RIALLM_OK;
 }
 

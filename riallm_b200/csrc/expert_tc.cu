@@ -121,6 +121,12 @@ struct Params {
   int d_cols;     // 64 or 128 accumulator columns per operand
   float* sk_ws;   // split-tile partial sums, one [2][d_cols][128] f32 slot per CTA; null: whole tiles
   int* sk_flags;  // one counter per CTA, zero between launches
+  // Bound (ns) of a split-tile owner's wait for the other CTAs' partial
+  // sums, and a count added to the awaited value (0; the test hook
+  // riallm_cuda_ctx_expire_next_wait sets one that is never reached, so the
+  // bounded wait expires and the launch reports RIALLM_ERR_TIMEOUT).
+  uint64_t flag_wait_ns;
+  int flag_extra;
   // The next launch's shape, for the L2 prefetch of its first stages
   // (pf_K == 0: no prefetch).
   int pf_K, pf_rows_per_expert, pf_a1_offset, pf_m_step, pf_m_tiles, pf_sk;
@@ -242,8 +248,9 @@ __device__ __forceinline__ bool sched_next(Sched& sc, Item& it, const int* tile_
 }
 
 // Bounded wait until *flag >= target (another CTA's partial sums are
-// published); false on abort or after kWaitLimitNs.
-__device__ __forceinline__ bool wait_flag(const int* flag, int target, volatile int* abort, int* status) {
+// published); false on abort or after limit_ns.
+__device__ __forceinline__ bool wait_flag(const int* flag, int target, volatile int* abort, int* status,
+                                          uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 0;; ++it) {
     int v;
@@ -251,7 +258,7 @@ __device__ __forceinline__ bool wait_flag(const int* flag, int target, volatile 
     if (v >= target) return true;
     if ((it & 15u) == 15u) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort = 1;
         atomicExch(status, 6 /* RIALLM_ERR_TIMEOUT */);
         return false;
@@ -849,7 +856,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (s0 >= tile_end) break;
           if (W * (b2 + 1) / G == s0) continue;
           int got = 1;
-          if (lane == 0) got = wait_flag(p.sk_flags + b2, kEpiWarps, abort_s, p.status) ? 1 : 0;
+          if (lane == 0)
+            got = wait_flag(p.sk_flags + b2, kEpiWarps + p.flag_extra, abort_s, p.status, p.flag_wait_ns) ? 1 : 0;
           ok = __shfl_sync(0xffffffffu, got, 0) != 0;
         }
         if (!ok) break;
@@ -1052,12 +1060,38 @@ cudaError_t launch_tc_gemm(const TcGemmArgs& a, int num_sms, cudaStream_t stream
                              (uint64_t)a.P, (uint64_t)a.K * 2, 64, Ns[i],
                              CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
-  tc::Params p{a.w.scales, a.w.zero_points, a.w.n_scales, a.w.n_zero_points, a.K,
-               a.rows_per_expert, a.a1_offset, a.m_step, a.m_tiles, a.counts, a.offsets, a.E,
-               a.swiglu ? 1 : 0, a.h_pair_perm ? 1 : 0, a.h_out, a.y_out, a.ld_out, a.status,
-               a.max_pairs_per_expert <= 64 ? 64 : 128, a.sk_ws, a.sk_flags,
-               pf ? nx->K : 0, pf ? nx->rows_per_expert : 0, pf ? nx->a1_offset : 0,
-               pf ? nx->m_step : 0, pf ? nx->m_tiles : 0, pf && nx->sk_ws != nullptr ? 1 : 0};
+  // Member by member: a positional initializer would silently shift
+  // values when a field is added.
+  tc::Params p{};
+  p.scales = a.w.scales;
+  p.zeros = a.w.zero_points;
+  p.n_scales = a.w.n_scales;
+  p.n_zeros = a.w.n_zero_points;
+  p.K = a.K;
+  p.rows_per_expert = a.rows_per_expert;
+  p.a1_offset = a.a1_offset;
+  p.m_step = a.m_step;
+  p.m_tiles = a.m_tiles;
+  p.counts = a.counts;
+  p.offsets = a.offsets;
+  p.E = a.E;
+  p.swiglu = a.swiglu ? 1 : 0;
+  p.h_pair_perm = a.h_pair_perm ? 1 : 0;
+  p.h_out = a.h_out;
+  p.y_out = a.y_out;
+  p.ld_out = a.ld_out;
+  p.status = a.status;
+  p.d_cols = a.max_pairs_per_expert <= 64 ? 64 : 128;
+  p.sk_ws = a.sk_ws;
+  p.sk_flags = a.sk_flags;
+  p.flag_wait_ns = a.flag_wait_ns ? a.flag_wait_ns : kWaitLimitNs;
+  p.flag_extra = a.flag_extra;
+  p.pf_K = pf ? nx->K : 0;
+  p.pf_rows_per_expert = pf ? nx->rows_per_expert : 0;
+  p.pf_a1_offset = pf ? nx->a1_offset : 0;
+  p.pf_m_step = pf ? nx->m_step : 0;
+  p.pf_m_tiles = pf ? nx->m_tiles : 0;
+  p.pf_sk = pf && nx->sk_ws != nullptr ? 1 : 0;
   auto kern = nf4 ? tc::expert_gemm_kernel<RIALLM_COMPRESSION_FOUR_BIT>
                   : tc::expert_gemm_kernel<RIALLM_COMPRESSION_EIGHT_BIT>;
   // Set the shared-memory opt-in once per device and variant, outside any

@@ -39,6 +39,11 @@ struct riallm_ctx {
   std::vector<PhaseEvents> pending;
   std::vector<cudaEvent_t> event_pool;
   uint64_t profiled_calls = 0;
+  // Bound (ns) of a kernel's wait for work published by other CTAs of the
+  // same launch (riallm_cuda_ctx_set_wait_limit; 0 = the default 1 s), and
+  // the test hook that makes the next MoE call's such wait expire.
+  uint64_t flag_wait_ns = 0;
+  bool expire_next_wait = false;
 };
 
 namespace rl {
@@ -173,6 +178,10 @@ struct TcGemmArgs {
   // prefetches into L2 the first weight stages that the same CTA index
   // reads in the next launch.
   const TcGemmArgs* next = nullptr;
+  // Bound of the split-tile owner's wait for partial sums (0: the default,
+  // kWaitLimitNs) and a count added to the awaited value (test hook).
+  uint64_t flag_wait_ns = 0;
+  int flag_extra = 0;
 };
 // Bytes of the split-tile workspace of launch_tc_gemm: one slot of
 // 2 operands x 128 rows x (64 or 128) f32 columns per CTA (= per SM).

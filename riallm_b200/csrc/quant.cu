@@ -2,8 +2,11 @@
 //
 // Bit-identical to riallm's host loops (src/quantization.rs). Every float
 // step uses an explicit round-to-nearest intrinsic so the compiler cannot
-// fuse or reorder it. HBM-bound: 16-byte loads and stores, grid sized in
-// multiples of the SM count.
+// fuse or reorder it. Dequantization is HBM-bound: a warp reads contiguous
+// codes and writes contiguous 16-byte vectors. Quantization stages blocks
+// in shared memory so that its global loads and stores are coalesced while
+// each block is still reduced in the reference's sequential order. Grids
+// are sized in multiples of the SM count.
 #include "common.cuh"
 #include "internal.h"
 
@@ -116,6 +119,73 @@ __global__ void copy_f32_kernel(const float* __restrict__ src, uint64_t n, OutT*
     store_val(out, i, src[i]);
 }
 
+// Eight consecutive outputs: two 16-byte stores of float32 or one of bf16
+// (dst 16-byte aligned).
+__device__ __forceinline__ void store8(float* out, uint64_t e0, const float (&v)[8]) {
+  float4* o = reinterpret_cast<float4*>(out + e0);
+  o[0] = make_float4(v[0], v[1], v[2], v[3]);
+  o[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* out, uint64_t e0, const float (&v)[8]) {
+  uint4 w;
+  w.x = pack_bf16x2(v[0], v[1]);
+  w.y = pack_bf16x2(v[2], v[3]);
+  w.z = pack_bf16x2(v[4], v[5]);
+  w.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(out + e0) = w;
+}
+
+// NF4, 64-element blocks (the format's block size), coalesced: thread i of
+// the grid-stride loop decodes elements 8i .. 8i+7 from one 4-byte word of
+// codes, so a warp reads 128 contiguous bytes and writes 1 KiB (float32) or
+// 512 bytes (bf16) contiguous with 16-byte stores. Elements 8i .. 8i+6 use
+// block (8i+1)/64 = 8i/64; element 8i+7 uses (8i+8)/64, the next block when
+// it is element 63 of its block (src/quantization.rs:55-72). Same arithmetic
+// as dq_value. Requires numel % 8 == 0 and 4-/16-byte aligned data / out.
+template <typename OutT>
+__global__ void __launch_bounds__(256) dequant_nf4_b64_kernel(DqParams p, OutT* __restrict__ out) {
+  const uint64_t nw = p.numel / 8;
+  const uint32_t* codes = reinterpret_cast<const uint32_t*>(p.data);
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < nw; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t w = __ldg(codes + i);
+    const uint64_t b0 = i >> 3, b7 = (8 * i + 8) >> 6;
+    const float s0 = b0 < p.n_scales ? __ldg(p.scales + b0) : 1.0f;
+    const float z0 = b0 < p.n_zeros ? __ldg(p.zeros + b0) : 0.0f;
+    const float s7 = b7 < p.n_scales ? __ldg(p.scales + b7) : 1.0f;
+    const float z7 = b7 < p.n_zeros ? __ldg(p.zeros + b7) : 0.0f;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t q = (w >> (4 * j)) & 15u;
+      const float s = j == 7 ? s7 : s0, z = j == 7 ? z7 : z0;
+      if (p.mode == 0) v[j] = __fmul_rn(__fsub_rn((float)q, z), s);
+      else v[j] = __fmul_rn(kNf4Table[q], s);
+    }
+    store8(out, 8 * i, v);
+  }
+}
+
+// 8-bit, 128-element blocks, coalesced: thread i decodes elements 8i .. 8i+7
+// (one 8-byte load, one block e/128 for all eight).
+template <typename OutT>
+__global__ void __launch_bounds__(256) dequant_int8_b128_kernel(DqParams p, OutT* __restrict__ out) {
+  const uint64_t nw = p.numel / 8;
+  const uint2* codes = reinterpret_cast<const uint2*>(p.data);
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < nw; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint2 c = __ldg(codes + i);
+    const uint64_t b = i >> 4;
+    const float s = b < p.n_scales ? __ldg(p.scales + b) : 1.0f;
+    const float z = b < p.n_zeros ? __ldg(p.zeros + b) : 0.0f;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float q = (float)(((j < 4 ? c.x : c.y) >> (8 * (j & 3))) & 255u);
+      v[j] = p.mode == 0 ? __fmul_rn(__fsub_rn(q, z), s) : __fadd_rn(__fmul_rn(q, s), z);
+    }
+    store8(out, 8 * i, v);
+  }
+}
+
 // --------------------------------------------------------------- quantize
 
 // src/quantization.rs:179-196: nearest code to clamp(v,-1,1), strict < so
@@ -137,60 +207,130 @@ __device__ __forceinline__ uint32_t nf4_code(float value) {
   return q;
 }
 
-// One thread per 64-element block (src/quantization.rs:132-166): absmax,
-// sequential f32 sum from -0.0, mean = sum / len, codes packed two per byte
-// (second element in the high nibble; an odd tail pads with code(0.0)).
-__global__ void quant_nf4_kernel(const float* __restrict__ v, uint64_t n, uint8_t* __restrict__ data,
-                                 float* __restrict__ scales, float* __restrict__ zeros) {
-  const uint64_t nb = (n + 63) / 64;
-  for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nb;
-       b += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t start = b * 64;
-    const uint32_t len = (uint32_t)min((uint64_t)64, n - start);
-    const float* blk = v + start;
-    float abs_max = 0.0f;
-    float sum = -0.0f;
-    for (uint32_t i = 0; i < len; ++i) {
-      float x = blk[i];
-      abs_max = fmaxf(abs_max, fabsf(x));
-      sum = __fadd_rn(sum, x);
+// Both quantizers stage a tile of kQBlocks blocks of the input in shared
+// memory with coalesced loads (rows padded by one float, so that thread t
+// walking block t sequentially hits bank (t + i) % 32), then thread t
+// quantizes block t in the reference's element order, and the codes go back
+// to global memory coalesced through shared memory.
+constexpr int kQBlocks = 128;
+
+__device__ __forceinline__ void stage_tile(const float* __restrict__ v, uint64_t n, uint64_t e_begin,
+                                           uint32_t count, uint32_t row, float* tile) {
+  // count elements from e_begin into rows of `row` floats (+1 padding).
+  const bool vec = ((reinterpret_cast<uintptr_t>(v + e_begin) & 15) == 0) && (count % 4 == 0);
+  if (vec) {
+    for (uint32_t i = threadIdx.x; i < count / 4; i += blockDim.x) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(v + e_begin) + i);
+      const uint32_t e = 4 * i, r = e / row, c = e % row;  // row % 4 == 0: a float4 stays in one row
+      float* d = tile + r * (row + 1) + c;
+      d[0] = f.x;
+      d[1] = f.y;
+      d[2] = f.z;
+      d[3] = f.w;
     }
-    scales[b] = __fdiv_rn(abs_max, 1.0f);
-    zeros[b] = __fdiv_rn(sum, (float)len);
-    uint8_t* o = data + start / 2;
-    for (uint32_t i = 0; i < len; i += 2) {
-      uint32_t q1 = nf4_code(blk[i]);
-      uint32_t q2 = nf4_code(i + 1 < len ? blk[i + 1] : 0.0f);
-      o[i / 2] = (uint8_t)((q2 << 4) | q1);
-    }
+  } else {
+    for (uint32_t e = threadIdx.x; e < count; e += blockDim.x) tile[(e / row) * (row + 1) + e % row] = v[e_begin + e];
   }
 }
 
-// One thread per 128-element block (src/quantization.rs:214-235):
-// scale = (max - min) / 255, zero = min, code = clamp(round((v - zero) /
-// scale), 0, 255) with Rust's saturating `as u8` (NaN -> 0).
-__global__ void quant_int8_kernel(const float* __restrict__ v, uint64_t n, uint8_t* __restrict__ data,
-                                  float* __restrict__ scales, float* __restrict__ zeros) {
-  const uint64_t nb = (n + 127) / 128;
-  for (uint64_t b = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; b < nb;
-       b += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t start = b * 128;
-    const uint32_t len = (uint32_t)min((uint64_t)128, n - start);
-    const float* blk = v + start;
-    float mn = __int_as_float(0x7f800000), mx = __int_as_float(0xff800000);
-    for (uint32_t i = 0; i < len; ++i) mn = fminf(mn, blk[i]);
-    for (uint32_t i = 0; i < len; ++i) mx = fmaxf(mx, blk[i]);
-    const float scale = __fdiv_rn(__fsub_rn(mx, mn), 255.0f);
-    scales[b] = scale;
-    zeros[b] = mn;
-    for (uint32_t i = 0; i < len; ++i) {
-      float t = roundf(__fdiv_rn(__fsub_rn(blk[i], mn), scale));
-      uint8_t q;
-      if (t != t || t <= 0.0f) q = 0;
-      else if (t >= 255.0f) q = 255;
-      else q = (uint8_t)t;
-      data[start + i] = q;
+// NF4 (src/quantization.rs:132-166): absmax, sequential float32 sum from
+// -0.0, mean = sum / len, codes packed two per byte (second element in the
+// high nibble; an odd tail pads with code(0.0)).
+__global__ void __launch_bounds__(kQBlocks) quant_nf4_kernel(const float* __restrict__ v, uint64_t n,
+                                                             uint8_t* __restrict__ data, float* __restrict__ scales,
+                                                             float* __restrict__ zeros) {
+  __shared__ float tile[kQBlocks * 65];
+  __shared__ uint32_t words[kQBlocks * 9];  // 8 code words per block, padded to 9
+  const uint64_t nb = (n + 63) / 64;
+  const int t = threadIdx.x;
+  for (uint64_t b0 = (uint64_t)blockIdx.x * kQBlocks; b0 < nb; b0 += (uint64_t)gridDim.x * kQBlocks) {
+    const uint32_t nblk = (uint32_t)min((uint64_t)kQBlocks, nb - b0);
+    const uint64_t e_begin = b0 * 64;
+    const uint32_t count = (uint32_t)min((uint64_t)nblk * 64, n - e_begin);
+    stage_tile(v, n, e_begin, count, 64, tile);
+    __syncthreads();
+    if ((uint32_t)t < nblk) {
+      const uint32_t len = min(64u, count - 64u * t);
+      const float* blk = tile + t * 65;
+      float abs_max = 0.0f;
+      float sum = -0.0f;
+      for (uint32_t i = 0; i < len; ++i) {
+        const float x = blk[i];
+        abs_max = fmaxf(abs_max, fabsf(x));
+        sum = __fadd_rn(sum, x);
+      }
+      scales[b0 + t] = __fdiv_rn(abs_max, 1.0f);
+      zeros[b0 + t] = __fdiv_rn(sum, (float)len);
+      for (uint32_t wi = 0; wi < 8; ++wi) {
+        uint32_t word = 0;
+        for (uint32_t k = 0; k < 8; ++k) {
+          const uint32_t i = 8 * wi + k;
+          // the odd tail's pad nibble is code(0.0); bytes past the data end are not stored
+          const uint32_t q = i < len ? nf4_code(blk[i]) : (i == len && (len & 1) ? nf4_code(0.0f) : 0u);
+          word |= q << (4 * k);
+        }
+        words[t * 9 + wi] = word;
+      }
     }
+    __syncthreads();
+    const uint32_t nbytes = (count + 1) / 2;
+    uint8_t* dst = data + e_begin / 2;
+    for (uint32_t i = t; i < nbytes; i += blockDim.x) {
+      const uint32_t blk = i / 32, off = i % 32;
+      dst[i] = (uint8_t)(words[blk * 9 + off / 4] >> (8 * (off % 4)));
+    }
+    __syncthreads();
+  }
+}
+
+// 8-bit (src/quantization.rs:214-235): scale = (max - min) / 255, zero = min,
+// code = clamp(round((v - zero) / scale), 0, 255) with Rust's saturating
+// `as u8` (NaN -> 0).
+__global__ void __launch_bounds__(kQBlocks / 2) quant_int8_kernel(const float* __restrict__ v, uint64_t n,
+                                                                  uint8_t* __restrict__ data,
+                                                                  float* __restrict__ scales,
+                                                                  float* __restrict__ zeros) {
+  constexpr int kB = kQBlocks / 2;  // 64 blocks of 128 per tile
+  __shared__ float tile[kB * 129];
+  __shared__ uint32_t words[kB * 33];  // 32 code words per block, padded to 33
+  const uint64_t nb = (n + 127) / 128;
+  const int t = threadIdx.x;
+  for (uint64_t b0 = (uint64_t)blockIdx.x * kB; b0 < nb; b0 += (uint64_t)gridDim.x * kB) {
+    const uint32_t nblk = (uint32_t)min((uint64_t)kB, nb - b0);
+    const uint64_t e_begin = b0 * 128;
+    const uint32_t count = (uint32_t)min((uint64_t)nblk * 128, n - e_begin);
+    stage_tile(v, n, e_begin, count, 128, tile);
+    __syncthreads();
+    if ((uint32_t)t < nblk) {
+      const uint32_t len = min(128u, count - 128u * t);
+      const float* blk = tile + t * 129;
+      float mn = __int_as_float(0x7f800000), mx = __int_as_float(0xff800000);
+      for (uint32_t i = 0; i < len; ++i) mn = fminf(mn, blk[i]);
+      for (uint32_t i = 0; i < len; ++i) mx = fmaxf(mx, blk[i]);
+      const float scale = __fdiv_rn(__fsub_rn(mx, mn), 255.0f);
+      scales[b0 + t] = scale;
+      zeros[b0 + t] = mn;
+      for (uint32_t wi = 0; wi < 32; ++wi) {
+        uint32_t word = 0;
+        for (uint32_t k = 0; k < 4; ++k) {
+          const uint32_t i = 4 * wi + k;
+          uint32_t q = 0;
+          if (i < len) {
+            const float r = roundf(__fdiv_rn(__fsub_rn(blk[i], mn), scale));
+            q = (r != r || r <= 0.0f) ? 0u : r >= 255.0f ? 255u : (uint32_t)r;
+          }
+          word |= q << (8 * k);
+        }
+        words[t * 33 + wi] = word;
+      }
+    }
+    __syncthreads();
+    uint8_t* dst = data + e_begin;
+    for (uint32_t i = t; i < count; i += blockDim.x) {
+      const uint32_t blk = i / 128, off = i % 128;
+      dst[i] = (uint8_t)(words[blk * 33 + off / 4] >> (8 * (off % 4)));
+    }
+    __syncthreads();
   }
 }
 
@@ -215,6 +355,25 @@ cudaError_t launch_dequant(const riallm_qtensor& t, int mode, void* dst, int dst
   }
   DqParams p{(const uint8_t*)t.data, t.scales, t.zero_points, t.n_scales, t.n_zero_points,
              t.numel, (uint32_t)t.block_size, mode};
+  const uintptr_t da = reinterpret_cast<uintptr_t>(t.data), oa = reinterpret_cast<uintptr_t>(dst);
+  const bool nf4 = t.qtype == RIALLM_COMPRESSION_FOUR_BIT;
+  // The format's own block sizes, whole 8-element groups and aligned
+  // buffers take the coalesced kernels; anything else the general ones.
+  if (t.numel % 8 == 0 && (oa & 15) == 0 && (da & (nf4 ? 3 : 7)) == 0 && t.block_size == (nf4 ? 64 : 128)) {
+    const int g = grid_for(t.numel / 8, threads, num_sms);
+    if (nf4) {
+      if (dst_dtype == RIALLM_DTYPE_F32)
+        dequant_nf4_b64_kernel<<<g, threads, 0, stream>>>(p, (float*)dst);
+      else
+        dequant_nf4_b64_kernel<<<g, threads, 0, stream>>>(p, (__nv_bfloat16*)dst);
+    } else {
+      if (dst_dtype == RIALLM_DTYPE_F32)
+        dequant_int8_b128_kernel<<<g, threads, 0, stream>>>(p, (float*)dst);
+      else
+        dequant_int8_b128_kernel<<<g, threads, 0, stream>>>(p, (__nv_bfloat16*)dst);
+    }
+    return cudaGetLastError();
+  }
   if (t.qtype == RIALLM_COMPRESSION_FOUR_BIT) {
     int g = grid_for((t.numel + 31) / 32, threads, num_sms);
     if (dst_dtype == RIALLM_DTYPE_F32)
@@ -233,13 +392,12 @@ cudaError_t launch_dequant(const riallm_qtensor& t, int mode, void* dst, int dst
 
 cudaError_t launch_quantize(int qtype, const float* src, uint64_t n, uint8_t* data, float* scales,
                             float* zeros, int num_sms, cudaStream_t stream) {
-  const int threads = 128;
   if (qtype == RIALLM_COMPRESSION_FOUR_BIT) {
-    quant_nf4_kernel<<<grid_for((n + 63) / 64, threads, num_sms), threads, 0, stream>>>(
-        src, n, data, scales, zeros);
+    const uint64_t tiles = ((n + 63) / 64 + kQBlocks - 1) / kQBlocks;
+    quant_nf4_kernel<<<grid_for(tiles, 1, num_sms), kQBlocks, 0, stream>>>(src, n, data, scales, zeros);
   } else {
-    quant_int8_kernel<<<grid_for((n + 127) / 128, threads, num_sms), threads, 0, stream>>>(
-        src, n, data, scales, zeros);
+    const uint64_t tiles = ((n + 127) / 128 + kQBlocks / 2 - 1) / (kQBlocks / 2);
+    quant_int8_kernel<<<grid_for(tiles, 1, num_sms), kQBlocks / 2, 0, stream>>>(src, n, data, scales, zeros);
   }
   return cudaGetLastError();
 }
