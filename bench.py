@@ -861,7 +861,8 @@ def fine_grained_measure(rb, torch, device, steps=20):
         bpw = 0.625 if qt == rb.CompressionType.FourBit else 1.0 + 8.0 / 128.0
         run = {"qtype": qt.name, "tokens": T, "tokens_per_s": round(T * steps / (ms / 1000.0), 1),
                "ms_per_step": round(ms / steps, 4), "distinct_experts": U,
-               "max_pairs_per_expert": int(counts.max().item()), "kernel_ms": round(kern_ms, 4)}
+               "max_pairs_per_expert": int(counts.max().item()), "kernel_ms": round(kern_ms, 4),
+               "phase_ms": {k: round(v, 4) for k, v in ph.items()}}
         if zipf:
             run["router"] = "float32 with a Zipf(1.1) expert-popularity bias"
         if T <= 512:
@@ -927,6 +928,10 @@ def parse_args(argv=None):
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--no-stream", action="store_true", help="skip the layer-streaming measurement")
     ap.add_argument("--no-decode", action="store_true", help="skip the Mixtral-8x7B decode measurement")
+    ap.add_argument("--quant-only", action="store_true",
+                    help="only the standalone quantize / dequantize measurement (prints {\"quant\": ...})")
+    ap.add_argument("--fine-grained-only", action="store_true",
+                    help="only the 128-expert top-8 measurement (prints {\"fine_grained\": ...})")
     ap.add_argument("--decode-only", action="store_true",
                     help="run only the Mixtral-8x7B decode measurement and print its JSON")
     ap.add_argument("--decode-batches", default="1,32", help="batch sizes of the decode measurement")
@@ -948,6 +953,18 @@ def main():
         torch.cuda.set_device(local)
         r = decode_measure(rb, torch, torch.device("cuda", local), decode_batches(args), new_tokens=args.decode_new)
         print(json.dumps({"decode": r}), flush=True)
+        return 0
+    if args.quant_only or args.fine_grained_only:
+        import torch
+        import riallm_b200 as rb
+        torch.cuda.set_device(local)
+        device = torch.device("cuda", local)
+        hbm_peak, _, _, peak_src = load_peaks()
+        if args.quant_only:
+            r = quant_measure(rb, torch, device, make_layer(rb, torch, device), hbm_peak, peak_src)
+            print(json.dumps({"quant": r}), flush=True)
+        else:
+            print(json.dumps({"fine_grained": fine_grained_measure(rb, torch, device)}), flush=True)
         return 0
     return run_ours(args, rank, world, local)
 

@@ -148,6 +148,7 @@ MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int share
   L.offsets = take((uint64_t)(E + 1) * 4);
   L.perm_pair = take(P * 4);
   L.inv_pos = take(P * 4);
+  L.cta_base = take((int64_t)P > kSortOneCta ? router_cta_bytes(T, H, E) : 0);
   L.x_perm = take(P * H * esz);
   L.h_perm = take(P * I * esz);
   L.y_perm = take(P * H * 4);
@@ -403,6 +404,7 @@ static int route_into(riallm_ctx* ctx, const riallm_qtensor& gate, const void* x
   a.perm_pair = (int*)(base + L.perm_pair);
   a.inv_pos = (int*)(base + L.inv_pos);
   a.done = (unsigned*)(base + L.sync);
+  a.cta_base = (int*)(base + L.cta_base);
   RL_CUDA(ctx, rl::launch_router(a, gate.qtype, st), "router");
   return RIALLM_OK;
 }

@@ -69,6 +69,7 @@ constexpr uint64_t kSkFlagsOffset = 256;
 struct MoeLayout {
   uint64_t sync, sk_ws, topk_idx, topk_w, counts, offsets, perm_pair, inv_pos;
   uint64_t x_perm, h_perm, y_perm, proj;
+  uint64_t cta_base;  // router per-CTA pair bases (multi-CTA sort)
   uint64_t sh_g, sh_u, sh_h, sh_y, sh_gate;
   uint64_t total;
 };
@@ -99,7 +100,20 @@ struct RouterArgs {
   int* perm_pair;
   int* inv_pos;
   unsigned* done;  // zero between calls; the last CTA resets it
+  // Calls of more than kSortOneCta pairs: per router CTA and expert, the
+  // CTA's pair count, then the base of its pairs (router_cta_bytes()).
+  int* cta_base;
 };
+// Pairs (T * k) up to which the router's last CTA sorts all pairs by itself;
+// larger calls sort with every router CTA and a scatter kernel.
+constexpr int64_t kSortOneCta = 16384;
+constexpr int kMaxExperts = 256;
+// Tokens per router CTA (1 for decode-sized calls).
+int router_tile_tokens(int T, int H);
+inline uint64_t router_cta_bytes(int T, int H, int E) {
+  const int tt = router_tile_tokens(T, H);
+  return (uint64_t)((T + tt - 1) / tt) * E * 4;
+}
 cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stream);
 // Gathers token rows into expert-sorted pair order. pair_perm (bf16 only)
 // stores each group of 8 columns in the K order of the NF4 tensor-core

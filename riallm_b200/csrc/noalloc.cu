@@ -157,6 +157,7 @@ extern "C" int32_t riallm_cuda_moe_forward_noalloc(const riallm_moe_weights* w, 
   ra.perm_pair = perm;
   ra.inv_pos = inv;
   ra.done = reinterpret_cast<unsigned*>(base + L.sync);
+  ra.cta_base = reinterpret_cast<int*>(base + L.cta_base);
   if (rl::launch_router(ra, w->gate.qtype, st) != cudaSuccess ||
       rl::launch_gather(x, true, perm, k, P, H, base + L.x_perm,
                         w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st) != cudaSuccess)

@@ -173,11 +173,18 @@ __device__ __forceinline__ void prefetch_share(const void* base, uint64_t bytes)
   }
 }
 
-// One CTA per token: warp w computes the logits of experts w, w+8, ...
-// (decoding the router weight on the fly), warp 0 then takes the softmax
-// and the top k. The CTA that finishes last (a counter in device memory,
-// zero between calls and reset by that CTA) sorts all pairs by expert.
-template <int QT>
+// A CTA routes TT consecutive tokens: warp w computes the logits of experts
+// w, w+8, ... for all of them, decoding each 8-element chunk of the router
+// weight once and applying it to the TT staged token rows (each token's
+// fused multiply-add chain runs in exactly the per-token order above); warp
+// t (t < TT) then takes token t's softmax and top k. TT = 1 for decode-sized
+// calls (one CTA per token), 4 or 8 for prefills, where the router weight
+// would otherwise be decoded once per token. Pair sorting: for up to
+// kSortOneCta pairs the CTA that finishes last (a counter in device memory,
+// zero between calls and reset by that CTA) sorts all pairs by expert;
+// above it every CTA counts its own pairs per expert, the last CTA turns
+// those counts into per-CTA bases (scatter_kernel places the pairs).
+template <int QT, int TT>
 __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs a) {
   extern __shared__ float sm[];
   __shared__ int is_last;
@@ -196,110 +203,256 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs
   pdl_wait();  // x comes from the previous kernel; every output is read by earlier ones
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x;
   const int E = a.E, H = a.H, k = a.k;
-  float* lg = sm;
-  float* pr = sm + E;
-  // The token's row, as float32, staged once for the 8 warps (one round of
-  // independent 16-byte loads instead of a load chain per expert).
-  float* xs = sm + ((2 * E + (kRouterThreads / 32) * (E + 1) + E + 1 + 3) & ~3);
+  const int t0 = blockIdx.x * TT;
+  const int nt = min(TT, a.T - t0);
+  float* lg = sm;             // [TT][E] logits (then "taken" marks)
+  float* pr = sm + TT * E;    // [TT][E] probabilities
+  int* hist = reinterpret_cast<int*>(sm + 2 * TT * E);
+  int* off_s = hist + (kRouterThreads / 32) * (E + 1);
+  // The tile's token rows as float32, staged once (16-byte aligned).
+  float* xs = sm + ((2 * TT * E + (kRouterThreads / 32) * (E + 1) + E + 1 + 3) & ~3);
   const int nchunk = H >> 3;
-  const uint64_t xrow = (uint64_t)t * H;
-  for (int c = threadIdx.x; c < nchunk; c += kRouterThreads) {
-    float xv[8];
-    load_chunk8(a.x, a.x_bf16 != 0, xrow + 8ull * c, xv);
-    *reinterpret_cast<float4*>(xs + 8 * c) = make_float4(xv[0], xv[1], xv[2], xv[3]);
-    *reinterpret_cast<float4*>(xs + 8 * c + 4) = make_float4(xv[4], xv[5], xv[6], xv[7]);
+  for (int i = threadIdx.x; i < TT * nchunk; i += kRouterThreads) {
+    const int t = i / nchunk, c = i - t * nchunk;
+    float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (t < nt) load_chunk8(a.x, a.x_bf16 != 0, (uint64_t)(t0 + t) * H + 8ull * c, xv);
+    float* d = xs + (uint64_t)t * H + 8 * c;
+    *reinterpret_cast<float4*>(d) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+    *reinterpret_cast<float4*>(d + 4) = make_float4(xv[4], xv[5], xv[6], xv[7]);
   }
   __syncthreads();
   for (int e = warp; e < E; e += kRouterThreads / 32) {
-    float acc = 0.0f;
+    float acc[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
     const uint64_t grow = (uint64_t)e * H;
-#pragma unroll 8
+#pragma unroll 4
     for (int c = lane; c < nchunk; c += 32) {
-      float xv[8], wv[8];
-      const float4 x0 = *reinterpret_cast<const float4*>(xs + 8 * c);
-      const float4 x1 = *reinterpret_cast<const float4*>(xs + 8 * c + 4);
-      xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
-      xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
+      float wv[8];
       gate_chunk8<QT>(a, grow + 8ull * c, wv);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc = __fmaf_rn(xv[i], wv[i], acc);
+      for (int t = 0; t < TT; ++t) {
+        const float4 x0 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 8 * c);
+        const float4 x1 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 8 * c + 4);
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(xv[i], wv[i], acc[t]);
+      }
     }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(kFull, acc, off));
-    if (lane == 0) lg[e] = acc;
+    for (int t = 0; t < TT; ++t) {
+      float v = acc[t];
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(kFull, v, off));
+      if (lane == 0) lg[t * E + e] = v;
+    }
   }
   __syncthreads();
-  if (warp == 0) {
+  if (warp < nt) {
+    const int t = t0 + warp;
+    float* l = lg + warp * E;
+    float* q = pr + warp * E;
     float m = __int_as_float(0xff800000);
-    for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
+    for (int e = lane; e < E; e += 32) m = fmaxf(m, l[e]);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(kFull, m, off));
-    for (int e = lane; e < E; e += 32) pr[e] = own_expf(__fsub_rn(lg[e], m));
+    for (int e = lane; e < E; e += 32) q[e] = own_expf(__fsub_rn(l[e], m));
     __syncwarp();
-    if (lane == 0) {
-      float s = 0.0f;
-      for (int e = 0; e < E; ++e) s = __fadd_rn(s, pr[e]);
-      for (int e = 0; e < E; ++e) pr[e] = __fdiv_rn(pr[e], s);
-      // Stable descending selection: strict > keeps the lower index on ties.
-      // lg[] is reused as the "taken" mark.
-      for (int e = 0; e < E; ++e) lg[e] = 0.0f;
-      int sel[16];
-      float ssum = 0.0f;
+    // Sequential sum in expert order, then every lane divides its share.
+    float s = 0.0f;
+    if (lane == 0)
+      for (int e = 0; e < E; ++e) s = __fadd_rn(s, q[e]);
+    s = __shfl_sync(kFull, s, 0);
+    for (int e = lane; e < E; e += 32) q[e] = __fdiv_rn(q[e], s);
+    __syncwarp();
+    // Stable descending selection: the largest probability, ties to the
+    // lower expert index (what a scan with strict > from the lowest index
+    // keeps). Warp-parallel: lane l holds experts l, l+32, ...; each round
+    // takes the lane-local best and reduces (value, index) across the warp.
+    // A NaN makes that order partial, so then lane 0 scans as the reference
+    // does.
+    int* sel = reinterpret_cast<int*>(l);  // l[] is free now; sel[j] in its first k words
+    bool nan = false;
+    for (int e = lane; e < E; e += 32) nan |= q[e] != q[e];
+    if (!__any_sync(kFull, nan)) {
+      float v[kMaxExperts / 32];
+#pragma unroll
+      for (int i = 0; i < kMaxExperts / 32; ++i) v[i] = lane + 32 * i < E ? q[lane + 32 * i] : 0.0f;
+      uint32_t taken = 0;
+      for (int j = 0; j < k; ++j) {
+        float bv = 0.0f;
+        int be = -1;
+#pragma unroll
+        for (int i = 0; i < kMaxExperts / 32; ++i) {
+          const int e = lane + 32 * i;
+          if (e < E && !((taken >> i) & 1u) && (be < 0 || v[i] > bv)) {
+            bv = v[i];
+            be = e;
+          }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+          const float ov = __shfl_xor_sync(kFull, bv, off);
+          const int oe = __shfl_xor_sync(kFull, be, off);
+          if (oe >= 0 && (be < 0 || ov > bv || (ov == bv && oe < be))) {
+            bv = ov;
+            be = oe;
+          }
+        }
+        if ((be & 31) == lane) taken |= 1u << (be >> 5);
+        if (lane == 0) sel[j] = be;
+      }
+    } else if (lane == 0) {
+      uint32_t taken[kMaxExperts / 32] = {};
       for (int j = 0; j < k; ++j) {
         int best = -1;
         for (int e = 0; e < E; ++e) {
-          if (lg[e] != 0.0f) continue;
-          if (best < 0 || pr[e] > pr[best]) best = e;
+          if ((taken[e >> 5] >> (e & 31)) & 1u) continue;
+          if (best < 0 || q[e] > q[best]) best = e;
         }
-        lg[best] = 1.0f;
+        taken[best >> 5] |= 1u << (best & 31);
         sel[j] = best;
       }
-      for (int j = 0; j < k; ++j) ssum = __fadd_rn(ssum, pr[sel[j]]);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      float ssum = 0.0f;
+      for (int j = 0; j < k; ++j) ssum = __fadd_rn(ssum, q[sel[j]]);
       for (int j = 0; j < k; ++j) {
         a.topk_idx[(uint64_t)t * k + j] = sel[j];
-        if (a.topk_w) a.topk_w[(uint64_t)t * k + j] = __fdiv_rn(pr[sel[j]], ssum);
+        if (a.topk_w) a.topk_w[(uint64_t)t * k + j] = __fdiv_rn(q[sel[j]], ssum);
       }
-      __threadfence();
-      is_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
     }
   }
+  const bool big = (int64_t)a.T * k > kSortOneCta;
+  if (big) {
+    // This CTA's pairs per expert, for the multi-CTA sort.
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += kRouterThreads) off_s[e] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < nt * k; p += kRouterThreads)
+      atomicAdd(&off_s[__ldcg(a.topk_idx + (uint64_t)t0 * k + p)], 1);
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += kRouterThreads) a.cta_base[(uint64_t)blockIdx.x * E + e] = off_s[e];
+  }
+  __threadfence();  // this thread's outputs, before the CTA is counted done
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  int* hist = reinterpret_cast<int*>(sm + 2 * E);
-  int* off_s = hist + (kRouterThreads / 32) * (E + 1);
-  permute_block(a.topk_idx, a.T * k, E, a.counts, a.offsets, a.perm_pair, a.inv_pos, hist, off_s);
+  if (!big) {
+    permute_block(a.topk_idx, a.T * k, E, a.counts, a.offsets, a.perm_pair, a.inv_pos, hist, off_s);
+  } else {
+    // Expert-major, CTA-minor exclusive scan of the per-CTA counts: the
+    // pairs of CTA c with expert e start at base[c][e]. Thread e walks its
+    // column of CTAs twice (total, then running bases).
+    const int nc = gridDim.x;
+    for (int e = threadIdx.x; e < E; e += kRouterThreads) {
+      int tot = 0;
+      for (int c = 0; c < nc; ++c) tot += __ldcg(a.cta_base + (uint64_t)c * E + e);
+      off_s[e + 1] = tot;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      off_s[0] = 0;
+      for (int e = 0; e < E; ++e) off_s[e + 1] += off_s[e];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += kRouterThreads) {
+      a.counts[e] = off_s[e + 1] - off_s[e];
+      int b = off_s[e];
+      for (int c = 0; c < nc; ++c) {
+        int* cell = a.cta_base + (uint64_t)c * E + e;
+        const int h = __ldcg(cell);
+        *cell = b;
+        b += h;
+      }
+    }
+    for (int e = threadIdx.x; e <= E; e += kRouterThreads) a.offsets[e] = off_s[e];
+  }
   __syncthreads();
   if (threadIdx.x == 0) *a.done = 0u;
 }
 
-cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stream) {
-  if (a.T <= 0) return cudaSuccess;
-  // logits + probabilities, pair-sort histograms, then the staged x row
-  // (16-byte aligned: the first part is padded to a multiple of 4 words).
-  const size_t words = ((size_t)2 * a.E + (size_t)(kRouterThreads / 32) * (a.E + 1) + a.E + 1 + 3) & ~(size_t)3;
-  const size_t smem = (size_t)a.H * sizeof(float) + words * sizeof(float);
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+// Multi-CTA pair sort, second half: CTA c places the pairs of the router's
+// CTA c (tokens [c TT, (c + 1) TT)) in pair order at the bases the router
+// computed, ranking equal experts with match_any as permute_block does, so
+// every expert's pairs stay in ascending pair (= token) order.
+__global__ void __launch_bounds__(128) scatter_kernel(const int* __restrict__ topk_idx, int T, int k, int E,
+                                                      int TT, int* __restrict__ cta_base,
+                                                      int* __restrict__ perm_pair, int* __restrict__ inv_pos) {
+  pdl_wait();  // the router's bases are final
+  pdl_launch_dependents();
+  __shared__ int base[kMaxExperts];
+  const int c = blockIdx.x;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) base[e] = cta_base[(uint64_t)c * E + e];
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  const int p0 = c * TT * k, p1 = min(T, (c + 1) * TT) * k;
+  for (int b0 = p0; b0 < p1; b0 += 32) {
+    const int p = b0 + lane;
+    const bool valid = p < p1;
+    const unsigned act = __ballot_sync(kFull, valid);
+    if (valid) {
+      const int e = topk_idx[p];
+      const unsigned peers = __match_any_sync(act, e);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      const int pos = base[e] + rank;
+      perm_pair[pos] = p;
+      if (inv_pos) inv_pos[p] = pos;
+      __syncwarp(act);
+      if (rank == 0) base[e] += __popc(peers);
+    }
+    __syncwarp();
+  }
+}
+
+template <int TT>
+static cudaError_t launch_router_tt(const RouterArgs& a, int gate_qtype, size_t smem, cudaStream_t stream) {
+  const dim3 grid((a.T + TT - 1) / TT);
+  auto kn = router_kernel<RIALLM_COMPRESSION_NONE, TT>;
+  auto k4 = router_kernel<RIALLM_COMPRESSION_FOUR_BIT, TT>;
+  auto k8 = router_kernel<RIALLM_COMPRESSION_EIGHT_BIT, TT>;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(router_kernel<RIALLM_COMPRESSION_NONE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(router_kernel<RIALLM_COMPRESSION_FOUR_BIT>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(router_kernel<RIALLM_COMPRESSION_EIGHT_BIT>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k4, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  if (gate_qtype == RIALLM_COMPRESSION_FOUR_BIT)
-    return launch_pdl(router_kernel<RIALLM_COMPRESSION_FOUR_BIT>, dim3(a.T), dim3(kRouterThreads), smem, stream, a);
-  else if (gate_qtype == RIALLM_COMPRESSION_EIGHT_BIT)
-    return launch_pdl(router_kernel<RIALLM_COMPRESSION_EIGHT_BIT>, dim3(a.T), dim3(kRouterThreads), smem, stream, a);
-  else
-    return launch_pdl(router_kernel<RIALLM_COMPRESSION_NONE>, dim3(a.T), dim3(kRouterThreads), smem, stream, a);
+  cudaError_t e;
+  if (gate_qtype == RIALLM_COMPRESSION_FOUR_BIT) e = launch_pdl(k4, grid, dim3(kRouterThreads), smem, stream, a);
+  else if (gate_qtype == RIALLM_COMPRESSION_EIGHT_BIT) e = launch_pdl(k8, grid, dim3(kRouterThreads), smem, stream, a);
+  else e = launch_pdl(kn, grid, dim3(kRouterThreads), smem, stream, a);
+  if (e != cudaSuccess) return e;
+  if ((int64_t)a.T * a.k > kSortOneCta) {
+    e = launch_pdl(scatter_kernel, grid, dim3(128), 0, stream, (const int*)a.topk_idx, a.T, a.k, a.E, TT,
+                   a.cta_base, a.perm_pair, a.inv_pos);
+    if (e != cudaSuccess) return e;
+  }
   return cudaGetLastError();
+}
+
+int router_tile_tokens(int T, int H) {
+  if (T < 512) return 1;
+  return H <= 3072 ? 8 : 4;
+}
+
+cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stream) {
+  if (a.T <= 0) return cudaSuccess;
+  const int TT = router_tile_tokens(a.T, a.H);
+  // logits + probabilities of TT tokens, pair-sort histograms, then the
+  // staged x rows (16-byte aligned: the first part is padded to a multiple
+  // of 4 words).
+  const size_t words = ((size_t)2 * TT * a.E + (size_t)(kRouterThreads / 32) * (a.E + 1) + a.E + 1 + 3) & ~(size_t)3;
+  const size_t smem = (size_t)TT * a.H * sizeof(float) + words * sizeof(float);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  if ((int64_t)a.T * a.k > kSortOneCta && a.cta_base == nullptr) return cudaErrorInvalidValue;
+  if (TT == 8) return launch_router_tt<8>(a, gate_qtype, smem, stream);
+  if (TT == 4) return launch_router_tt<4>(a, gate_qtype, smem, stream);
+  return launch_router_tt<1>(a, gate_qtype, smem, stream);
 }
 
 // One warp per pair row; 16-byte copies. With pair_perm each 16-byte

@@ -34,6 +34,13 @@ def test_router_golden_bit_exact(rb):
     (50, 512, 16, 4, 1, False),     # float32 activations
     (200, 2048, 256, 16, 1, True),  # widest supported: 256 experts, top-16
     (7, 1024, 8, 2, 0, True),       # float32 router weight
+    # Prefill sizes: 8 (hidden <= 3072) or 4 tokens per router CTA, a ragged
+    # last tile, and above 16384 pairs the multi-CTA pair sort.
+    (1001, 2048, 128, 8, 1, True),
+    (2051, 2048, 128, 8, 2, True),  # 16408 pairs: multi-CTA sort, ragged tile
+    (517, 6144, 8, 2, 1, True),     # 4 tokens per CTA (hidden 6144)
+    (3000, 1024, 256, 16, 0, True),  # 48000 pairs, float32 router, 256 experts
+    (700, 512, 16, 4, 1, False),    # float32 activations, tiled
 ])
 def test_router_random_bit_exact(rb, oracle_lib, T, H, E, k, qt, bf16):
     O = oracle_lib
