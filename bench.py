@@ -12,8 +12,10 @@ tokens (default: a decode batch of 64). The weights are larger than the
 
 Prints ONE JSON line on rank 0. Multi-GPU (torchrun, one rank per GPU):
 expert parallel -- rank r keeps experts [r E/N, (r+1) E/N), every step
-all-gathers the ranks' batches (NCCL), runs its experts for all tokens and
-reduce-scatters the partial sums (weak scaling: 64 tokens per GPU); value
+routes its own batch, sends each token row to the ranks that own its
+experts and gets the expert outputs back (a token all-to-all inside the
+library over NCCL point-to-point), then sums them per token (weak scaling:
+64 tokens per GPU); value
 is the total tokens of all ranks over the slowest rank's device time.
 The single-GPU line also carries a Mixtral-8x7B decode measurement (32
 layers, batch 1 and 32; --decode-only runs it alone), a token-count sweep,
@@ -183,7 +185,9 @@ def config_dict(args, world):
     return {"workload": f"mixtral8x7b_moe_block_nf4_decode_T{args.tokens}",
             "hidden": H, "intermediate": I, "experts": E, "top_k": TOP_K,
             "tokens_per_step_per_gpu": args.tokens, "compression": "FourBit (riallm NF4 layout)",
-            "parallelism": f"ep{world} (expert-parallel: {E // max(world, 1)} experts per GPU, tokens all-gathered, partials reduce-scattered over NCCL)" if world > 1 else "single",
+            "parallelism": (f"ep{world} (expert-parallel: {E // max(world, 1)} experts per GPU; "
+                            + ("tokens all-gathered, partials reduce-scattered over NCCL)" if args.ep_path == "replicated"
+                               else "token all-to-all over NCCL inside the library)")) if world > 1 else "single",
             "l2_policy": "inputs larger than L2 (880.8 MB of NF4 weights per step vs 126 MB L2)"}
 
 
@@ -458,6 +462,7 @@ def run_ours(args, rank, world, local):
         cpu = cpu_baseline(rb, torch, d, blk)
     streaming = None if args.no_stream else stream_measure(rb, torch, d, blk.x)
     streaming_8x22b = None if args.no_stream else stream_measure_8x22b(rb, torch, device)
+    streaming_model = None if args.no_stream else stream_model_measure(rb, torch, device)
     decode = None if args.no_decode else decode_measure(rb, torch, device, decode_batches(args),
                                                         new_tokens=args.decode_new)
     fine = None if args.no_sweep else fine_grained_measure(rb, torch, device)
@@ -475,6 +480,7 @@ def run_ours(args, rank, world, local):
             "gpu_launches_note": f"{launches_per_step} kernels per step (router, gather, expert gate_up and down GEMMs, combine) replayed from one CUDA graph",
             "captured_launches": per_step_launches,
             "clocks": clk.summary(), "sweep": sweep, "streaming": streaming, "streaming_8x22b": streaming_8x22b,
+            "streaming_model": streaming_model,
             "decode": decode, "fine_grained": fine, "quant": quant,
         }
         print(json.dumps(line), flush=True)
@@ -487,43 +493,64 @@ def run_ours(args, rank, world, local):
 
 def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_src):
     """Expert parallel over `world` GPUs (weak scaling: args.tokens tokens per
-    GPU). Rank r keeps experts [r E/W, (r+1) E/W); a step all-gathers the
-    tokens, runs the local experts for all of them (riallm_cuda_moe_forward_ep)
-    and reduce-scatters the float32 partials (riallm_b200.ep)."""
-    from riallm_b200.ep import ExpertParallelMoE, expert_range
+    GPU); rank r keeps experts [r E/W, (r+1) E/W). Two designs are timed on
+    the same tokens, each checked against the single-GPU block:
+
+      replicated: all-gather the tokens, every rank runs its experts for all
+        of them (riallm_cuda_moe_forward_ep), reduce-scatter the float32
+        partials (riallm_b200.ep.ExpertParallelMoE; no host synchronisation);
+      all_to_all: each rank routes its own tokens and exchanges only the
+        routed rows and their expert outputs (riallm_cuda_moe_forward_ep_a2a,
+        NCCL inside the library; one host synchronisation per call for the
+        message sizes).
+
+    --ep-path picks the one the line's value, roofline and e2e report (the
+    replicated one by default: faster at decode batch sizes); the other is
+    reported beside it. Phase times come from the library's events; the
+    collectives of the replicated path run in torch, so its communication is
+    the step time minus the library phases."""
+    from riallm_b200.ep import ExpertParallelA2A, ExpertParallelMoE, expert_range
     e_b, e_l = expert_range(E, rank, world)
     local_w = {"mlp.gate.weight": d["mlp.gate.weight"],
                "mlp.experts.gate_up_proj": d["mlp.experts.gate_up_proj"].expert_slice(e_b, e_l),
                "mlp.experts.down_proj": d["mlp.experts.down_proj"].expert_slice(e_b, e_l)}
-    blk = ExpertParallelMoE(local_w, E, TOP_K)
     gen = torch.Generator(device=device).manual_seed(1000 + args.tokens + 7919 * rank)
     x = torch.empty(args.tokens, H, device=device).normal_(0, 1, generator=gen).to(torch.bfloat16)
-    ctx = rb.Context.get(device.index or 0)
-    ctx.reserve(world * args.tokens, H, I, E, TOP_K, torch.bfloat16)
-    out = None
-
-    def step():
-        nonlocal out
-        out = blk(x)
-    step()
-    l0 = ctx.launch_count()
-    step()
-    launches_per_step = ctx.launch_count() - l0  # library kernels of one step
-    with ClockSampler(local) as clk:
-        ms = timed(torch, step, args.steps, args.warmup, dist, world)
-    ms_per_step = ms / args.steps
-    value = world * args.tokens * args.steps / (ms / 1000.0)
+    ctx_rep = rb.Context(device.index or 0)
+    ctx_rep.reserve(world * args.tokens, H, I, E, TOP_K, torch.bfloat16)
+    rep = ExpertParallelMoE(local_w, E, TOP_K)
+    a2a = ExpertParallelA2A(local_w, E, TOP_K, device=local)
+    paths = {"replicated": (lambda v: rep(v, ctx=ctx_rep), ctx_rep),
+             "all_to_all": (a2a, a2a.ctx)}
+    head = args.ep_path
+    order = [head] + ([] if args.no_sweep else [p for p in paths if p != head])
+    res, clk = {}, None
+    for name in order:
+        fn, ctx = paths[name]
+        fn(x)
+        l0 = ctx.launch_count()
+        fn(x)
+        launches = ctx.launch_count() - l0  # library kernels of one step
+        if name == head:
+            with ClockSampler(local) as clk:
+                ms = timed(torch, lambda: fn(x), args.steps, args.warmup, dist, world)
+        else:
+            ms = timed(torch, lambda: fn(x), args.steps, args.warmup, dist, world)
+        ph = ep_phases(torch, _EpCall(fn, ctx), x, n=10)
+        lib_ms = sum(ph.values())
+        res[name] = {"tokens_per_s": round(world * args.tokens * args.steps / (ms / 1000.0), 1),
+                     "ms_per_step": round(ms / args.steps, 4), "launches_per_step": launches,
+                     "phase_ms_per_step": ph,
+                     "outside_library_ms_per_step": round(max(ms / args.steps - lib_ms, 0.0), 4),
+                     "check": ep_verify(rb, torch, dist, d, fn, x, rank, world)}
+    ms_per_step = res[head]["ms_per_step"]
+    value = res[head]["tokens_per_s"]
+    launches_per_step = res[head]["launches_per_step"]
+    ep_check = res[head]["check"]
+    blk = paths[head][0]
+    ph = res[head]["phase_ms_per_step"]
 
     # Local expert GEMM phases on this rank (roofline of the dominant kernel).
-    torch.cuda.synchronize()
-    ctx.profile(True)
-    torch.cuda._sleep(int(2e8))
-    for _ in range(10):
-        step()
-    torch.cuda.synchronize()
-    ctx.profile(False)
-    ph, calls = ctx.profile_read()
-    ph = {k: v / max(calls, 1) for k, v in ph.items()}
     parts = [torch.empty_like(x) for _ in range(world)]
     dist.all_gather(parts, x)
     _, _, counts, _, _ = rb.route(d["mlp.gate.weight"], torch.cat(parts, 0), TOP_K, E)
@@ -534,10 +561,10 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     achieved = bytes_step / (kern_ms / 1000.0) / 1e9 if kern_ms > 0 else 0.0
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": None,
-                "kernel": "expert_gemm_kernel<NF4> (rank 0's gate_up + down launches of one step)",
+                "kernel": f"expert_gemm_kernel<NF4> (rank 0's gate_up + down launches of one {head} step)",
                 "algorithmic_bytes_per_step": bytes_step, "distinct_experts": U_local,
                 "kernel_ms_per_step": round(kern_ms, 4),
-                "phase_ms_per_step": {k: round(v, 4) for k, v in ph.items()},
+                "phase_ms_per_step": ph,
                 "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else peak_src}
 
     # End to end: this rank's tokens from pinned host memory, the block, the
@@ -589,7 +616,11 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     tt = torch.tensor([t0.elapsed_time(t1)], device="cuda")
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     e2e_ms = float(tt.item())
-    ep_check = ep_verify(rb, torch, dist, d, blk, x, rank, world)
+    a2a.close()
+    ctx_rep.close()
+    fine_ep = None if args.no_sweep else ep_fine_measure(rb, torch, dist, device, rank, world)
+    dec_ep = None if args.no_decode else ep_decode_measure(rb, torch, dist, device, rank, world,
+                                                           decode_batches(args), new_tokens=min(args.decode_new, 64))
     nbytes = x.numel() * 2
     e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
@@ -604,32 +635,198 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
             "config": config_dict(args, world),
             "roofline": roofline, "cpu_baseline": None, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
-            "gpu_launches_note": f"{launches_per_step} library kernels per step per GPU (router, gather, expert gate_up and down GEMMs, partial combine) plus NCCL all-gather and reduce-scatter",
-            "clocks": clk.summary(), "sweep": [], "ep_check": ep_check,
+            "gpu_launches_note": f"{launches_per_step} library kernels per step per GPU ({head} path) plus its NCCL collectives",
+            "clocks": clk.summary(), "sweep": [], "ep_check": ep_check, "ep_path": head, "ep_paths": res,
+            "fine_grained_ep": fine_ep,
+            "decode": dec_ep,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
-    return 0 if ep_check["passed"] else 1
+    fine_ok = fine_ep is None or all(r["check"]["passed"] for r in fine_ep["runs"])
+    dec_ok = dec_ep is None or all(r["check"]["passed"] for r in dec_ep["runs"] if "check" in r)
+    paths_ok = all(r["check"]["passed"] for r in res.values())
+    return 0 if paths_ok and fine_ok and dec_ok else 1
 
 
 EP_TOL = 5e-3
 
 
+def ep_compare(torch, dist, out, ref):
+    """Expert-parallel output against the single-GPU block on the same
+    tokens, worst over the ranks. The two sum the same float32 terms in a
+    different order and round each output to bf16 once, so an element may
+    differ by one bf16 rounding step (up to 2^-7 of its magnitude) where the
+    float32 value sits next to a rounding boundary. Passes when every
+    element differs by at most one bf16 ulp of the larger of the two values
+    plus 1e-3 of max |single| (the float32 reordering itself, which matters
+    only for elements near zero): max |ep - single| / max |single| is then
+    below 2^-7 + 1e-3, and below EP_TOL when no large element flips."""
+    a, b = out.float(), ref.float()
+    diff = (a - b).abs()
+    _, ex = torch.frexp(torch.maximum(a.abs(), b.abs()))
+    ulp = torch.ldexp(torch.ones_like(diff), (ex - 8).to(torch.int32))
+    scale = b.abs().max()
+    bad = (diff > ulp + 1e-3 * scale).sum().float()
+    t = torch.stack([diff.max() / scale, (diff / ulp).max(), (diff > 0).sum().float() / diff.numel(), bad])
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    rel, ulps, frac, nbad = float(t[0]), float(t[1]), float(t[2]), int(t[3])
+    return {"max_rel_err": rel, "max_ulps": ulps, "frac_elements_differing": frac, "elements_beyond_bound": nbad,
+            "bound": "1 bf16 ulp + 1e-3 * max|single| per element", "passed": nbad == 0}
+
+
+def ep_phases(torch, blk, x, n=5):
+    """Mean per-phase device times (ms) of n expert-parallel steps, from the
+    library's events on the launching stream (route, gather, dispatch,
+    gate_up, down, return, combine; the counts exchange and its host
+    synchronisation are the rest of the step)."""
+    torch.cuda.synchronize()
+    blk.ctx.profile(True)
+    for _ in range(n):
+        blk(x)
+    torch.cuda.synchronize()
+    blk.ctx.profile(False)
+    ph, calls = blk.ctx.profile_read()
+    return {k: round(v / max(calls, 1), 4) for k, v in ph.items()}
+
+
+def ep_decode_measure(rb, torch, dist, device, rank, world, batches=(1, 32), prompt_len=512, new_tokens=64,
+                      seed=3):
+    """Mixtral-8x7B decoding (32 layers, synthetic weights seed 3 as in
+    decode_measure) expert parallel over the ranks: each rank keeps 8 / world
+    experts of every layer plus replicated attention, norms, embedding and LM
+    head, and decodes its own batch of sequences (prompt of `prompt_len` ids,
+    then `new_tokens` teacher-forced steps replayed from the decode graph);
+    every MoE block all-gathers the ranks' tokens and reduce-scatters the
+    partial sums (ExpertParallelMoE, NCCL, captured in the graph). Times are
+    the max over ranks; tok/s counts every rank's sequences. Rank 0 first runs
+    its first prefill on the whole model on one GPU and checks the
+    expert-parallel prefill logits against it."""
+    from riallm_b200 import decoder as D
+    from riallm_b200.ep import ExpertParallelMoE, expert_range
+    cfg = D.DecoderConfig.mixtral_8x7b()
+    dev = device.index or 0
+    t0 = time.perf_counter()
+    qw = D.synthetic_model(cfg, seed=seed, device=str(device))
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    g = torch.Generator().manual_seed(seed + 101 * rank)
+    prompts = {B: torch.randint(0, cfg.vocab, (B, prompt_len), generator=g).to(device) for B in batches}
+    conts = {B: torch.randint(0, cfg.vocab, (new_tokens, B, 1), generator=g).to(device) for B in batches}
+    ref_logits = None
+    if rank == 0:
+        full = D.Decoder(cfg, qw, max_batch=batches[0], max_seq=prompt_len + 1, device=dev)
+        ref_logits = full.forward(prompts[batches[0]]).float().cpu().numpy()
+        full.close()
+        del full
+    dist.barrier()
+    e_b, e_l = expert_range(cfg.experts, rank, world)
+    local = {}
+    for name, v in qw.items():
+        if ".mlp.experts." in name:
+            sl = v.expert_slice(e_b, e_l)
+            local[name] = rb.QuantizedTensor(sl.data.clone(), tuple(sl.shape), sl.qtype, sl.scales.clone(),
+                                             sl.zero_points.clone(), sl.block_size)
+        else:
+            local[name] = v
+    del qw
+    torch.cuda.empty_cache()
+    ep = ExpertParallelMoE(None, cfg.experts, cfg.top_k)
+    model = D.Decoder(cfg, local, max_batch=max(batches), max_seq=prompt_len + new_tokens + 3, device=dev, ep=ep)
+    del local
+    out = {"model": f"mixtral-8x7b: 32 layers, synthetic weights (seed {seed}), experts NF4 ({e_l} per GPU), "
+                    "attention/embedding bf16 replicated", "prompt_tokens": prompt_len, "new_tokens": new_tokens,
+           "build_s": round(build_s, 2), "runs": []}
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+    for B in batches:
+        model.generate(prompts[B], 2)  # warm-up: prefill shapes and the decode graph for B
+        model.reset()
+        p0, p1, d1 = ev(), ev(), ev()
+        dist.barrier()
+        torch.cuda.synchronize()
+        p0.record()
+        logits = model.forward(prompts[B])
+        p1.record()
+        model.decode_forced(conts[B])
+        d1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([p0.elapsed_time(p1), p1.elapsed_time(d1)], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pms, dms = float(t[0]), float(t[1])
+        run = {"batch_per_gpu": B, "decode_tok_s": round(world * B * new_tokens / (dms / 1000.0), 1),
+               "ms_per_decode_step": round(dms / new_tokens, 3), "prefill_ms": round(pms, 2),
+               "prefill_tok_s": round(world * B * prompt_len / (pms / 1000.0), 1)}
+        if rank == 0 and B == batches[0]:
+            lg = logits.float().cpu().numpy()
+            e = float(abs(lg - ref_logits).max() / abs(ref_logits).max())
+            run["check"] = {"prefill_logits_rel_err_vs_one_gpu": e, "tol": 2e-2, "passed": e < 2e-2}
+        out["runs"].append(run)
+    model.close()
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
+def ep_fine_measure(rb, torch, dist, device, rank, world, steps=10):
+    """The fine-grained block (hidden 2048, 128 experts, top-8, intermediate
+    768; N(0, 0.02) weights seed 4 quantized to NF4, as fine_grained_measure
+    makes them) expert parallel over the ranks, 128 / world experts each: a
+    64-token decode batch and an 8192-token prefill per rank. Step time is
+    the max over ranks; phase times are rank 0's; every rank's output is
+    checked against the single-GPU block on its own tokens (a token's output
+    depends on that token alone), within EP_TOL."""
+    from riallm_b200.ep import ExpertParallelA2A, expert_range
+    Hf, If, Ef, kf = 2048, 768, 128, 8
+    qt = rb.CompressionType.FourBit
+    g = torch.Generator(device=device).manual_seed(4)
+    d = {"mlp.gate.weight": rb.quantize_tensor(torch.randn(Ef, Hf, device=device, generator=g) * 0.02, qt),
+         "mlp.experts.gate_up_proj": rb.quantize_tensor(
+             torch.randn(Ef, 2 * If, Hf, device=device, generator=g) * 0.02, qt),
+         "mlp.experts.down_proj": rb.quantize_tensor(torch.randn(Ef, Hf, If, device=device, generator=g) * 0.02, qt)}
+    e_b, e_l = expert_range(Ef, rank, world)
+    local_w = {"mlp.gate.weight": d["mlp.gate.weight"],
+               "mlp.experts.gate_up_proj": d["mlp.experts.gate_up_proj"].expert_slice(e_b, e_l),
+               "mlp.experts.down_proj": d["mlp.experts.down_proj"].expert_slice(e_b, e_l)}
+    blk = ExpertParallelA2A(local_w, Ef, kf, device=device.index or 0)
+    out = {"config": f"fine-grained: hidden 2048, 128 experts, top-8, intermediate 768, NF4; {e_l} experts per GPU",
+           "runs": []}
+    for T in (64, 8192):
+        gx = torch.Generator(device=device).manual_seed(4000 + T + 7919 * rank)
+        x = torch.randn(T, Hf, device=device, generator=gx).to(torch.bfloat16)
+        ms = timed(torch, lambda: blk(x), steps, 3, dist, world)
+        ph = ep_phases(torch, blk, x)
+        chk = ep_compare(torch, dist, blk(x), rb.apply_moe(d, x, kf, Ef))
+        out["runs"].append({"tokens_per_gpu": T, "tokens_per_s": round(world * T * steps / (ms / 1000.0), 1),
+                            "ms_per_step": round(ms / steps, 4), "phase_ms_per_step": ph, "check": chk})
+    blk.close()
+    del d, local_w
+    torch.cuda.empty_cache()
+    return out
+
+
+class _EpCall:
+    """An expert-parallel step in the shape ep_phases expects."""
+
+    def __init__(self, fn, ctx):
+        self.fn, self.ctx = fn, ctx
+
+    def __call__(self, x):
+        return self.fn(x)
+
+
 def ep_verify(rb, torch, dist, d, blk, x, rank, world):
     """Checks the expert-parallel step's output on every rank against the
     single-GPU block run on the same gathered tokens (this rank holds the
-    whole layer): max |ep - single| / max |single| over each rank's tokens
-    within EP_TOL; the worst rank's error is reported."""
+    whole layer), with ep_compare; the worst rank's figures are reported."""
     out = blk(x)
     parts = [torch.empty_like(x) for _ in range(world)]
     dist.all_gather(parts, x)
     ref = rb.apply_moe(d, torch.cat(parts, 0), TOP_K, E)[rank * x.shape[0]:(rank + 1) * x.shape[0]]
-    err = ((out.float() - ref.float()).abs().max() / ref.float().abs().max()).reshape(1)
-    dist.all_reduce(err, op=dist.ReduceOp.MAX)
-    e = float(err.item())
-    return {"max_rel_err": e, "tol": EP_TOL, "passed": e < EP_TOL,
-            "against": "single-GPU riallm_cuda_moe_forward on the same gathered tokens, every rank"}
+    chk = ep_compare(torch, dist, out, ref)
+    chk["against"] = "single-GPU riallm_cuda_moe_forward on the same gathered tokens, every rank"
+    return chk
 
 
 def stream_measure(rb, torch, d, x, n_layers=4, depth=2, experts=E, top_k=TOP_K, label=None):
@@ -691,6 +888,80 @@ def stream_measure_8x22b(rb, torch, device, n_layers=2, tokens=16, seed=5):
     out = stream_measure(rb, torch, d, x, n_layers=n_layers,
                          label="mixtral-8x22b block (H 6144, I 16384, E 8, top-2, NF4)")
     del d
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return out
+
+
+def stream_model_measure(rb, torch, device, layers=4, batch=16, prompt_len=1024, new_tokens=64, seed=5, depth=2):
+    """Mixtral-8x22B decoding at reduced depth (hidden 6144, 48/8 heads,
+    intermediate 16384, 8 experts, top-2, V 32768; `layers` of the model's 56
+    layers; synthetic weights as in decode_measure, experts NF4) run twice:
+    with the MoE tensors resident in HBM (decode steps replayed from a graph)
+    and streamed from pinned host memory through `depth` device slots
+    (ModelOptions.prefetch_layers, eager steps). A batch of `batch` prompts
+    of `prompt_len` ids, then `new_tokens` teacher-forced decode steps.
+    exposed_copy_ms_per_layer = (streamed - resident) / layers: the part of
+    each layer's copy that the compute does not hide."""
+    from riallm_b200 import decoder as D
+    from riallm_b200.streaming import LayerStreamer, PackedLayer
+    cfg = D.DecoderConfig(layers=layers, hidden=6144, heads=48, kv_heads=8, head_dim=128, eps=1e-5, theta=1e6,
+                          vocab=32768, experts=8, top_k=2, intermediate=16384)
+    qw = D.synthetic_model(cfg, seed=seed, device=str(device))
+    names = ("mlp.gate.weight", "mlp.experts.gate_up_proj", "mlp.experts.down_proj")
+    ctx = rb.Context.get(device.index or 0)
+    packed = [PackedLayer({n: qw[f"model.layers.{l}.{n}"] for n in names}, ctx=ctx) for l in range(layers)]
+    streamer = LayerStreamer(packed, depth=depth, device=device.index or 0)
+    max_seq = prompt_len + new_tokens + 3
+    resident = D.Decoder(cfg, qw, max_batch=batch, max_seq=max_seq, device=device.index or 0)
+    streamed = D.Decoder(cfg, {k: v for k, v in qw.items() if ".mlp." not in k}, max_batch=batch,
+                         max_seq=max_seq, device=device.index or 0, streamer=streamer)
+    del qw
+    g = torch.Generator().manual_seed(seed)
+    prompt = torch.randint(0, cfg.vocab, (batch, prompt_len), generator=g).to(device)
+    cont = torch.randint(0, cfg.vocab, (new_tokens, batch, 1), generator=g).to(device)
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    def run(model):
+        model.generate(prompt, 2)  # warm-up: prefill shapes, scratch arenas, the decode graph
+        model.reset()
+        p0, p1, d1 = ev(), ev(), ev()
+        torch.cuda.synchronize()
+        p0.record()
+        model.forward(prompt)
+        p1.record()
+        model.decode_forced(cont)
+        d1.record()
+        torch.cuda.synchronize()
+        pms, dms = p0.elapsed_time(p1), p1.elapsed_time(d1)
+        return {"prefill_ms": round(pms, 2), "prefill_tok_s": round(batch * prompt_len / (pms / 1000.0), 1),
+                "ms_per_decode_step": round(dms / new_tokens, 3),
+                "decode_tok_s": round(batch * new_tokens / (dms / 1000.0), 1)}
+    r = run(resident)
+    b0 = streamer.stats()
+    s = run(streamed)
+    b1 = streamer.stats()
+    nbytes, copy_ms = b1["bytes"] - b0["bytes"], b1["copy_ms"] - b0["copy_ms"]
+    h2d = nbytes / (copy_ms / 1000.0) / 1e9 if copy_ms > 0 else 0.0
+    s["h2d_gbs"] = round(h2d, 2)
+    layer_bytes = packed[0].nbytes
+    out = {"model": f"mixtral-8x22b shapes, {layers} of 56 layers, synthetic weights (seed {seed}), experts NF4, "
+                    "attention/embedding bf16",
+           "batch": batch, "prompt_tokens": prompt_len, "new_tokens": new_tokens, "prefetch_buffer_size": depth,
+           "layer_bytes": layer_bytes, "resident": r, "streamed": s,
+           "copy_ms_per_layer": round(layer_bytes / h2d / 1e6, 3) if h2d else None,
+           "exposed_copy_ms_per_layer_decode": round((s["ms_per_decode_step"] - r["ms_per_decode_step"]) / layers, 3),
+           "exposed_copy_ms_per_layer_prefill": round((s["prefill_ms"] - r["prefill_ms"]) / layers, 3),
+           "note": "streamed: every forward copies each layer's router + experts from pinned host memory while the "
+                   "previous layer computes; resident decode steps are graph replays, streamed ones eager"}
+    resident.close()
+    streamed.close()
+    streamer.close()
+    for p in packed:
+        p.close()
+    del resident, streamed
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return out
@@ -924,6 +1195,8 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--ep-path", choices=("replicated", "all_to_all"), default="replicated",
+                    help="expert-parallel design the multi-GPU line reports (the other is timed beside it)")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--no-stream", action="store_true", help="skip the layer-streaming measurement")
@@ -932,6 +1205,8 @@ def parse_args(argv=None):
                     help="only the standalone quantize / dequantize measurement (prints {\"quant\": ...})")
     ap.add_argument("--fine-grained-only", action="store_true",
                     help="only the 128-expert top-8 measurement (prints {\"fine_grained\": ...})")
+    ap.add_argument("--stream-model-only", action="store_true",
+                    help="only the reduced-depth streamed Mixtral-8x22B decode (prints {\"streaming_model\": ...})")
     ap.add_argument("--decode-only", action="store_true",
                     help="run only the Mixtral-8x7B decode measurement and print its JSON")
     ap.add_argument("--decode-batches", default="1,32", help="batch sizes of the decode measurement")
@@ -953,6 +1228,13 @@ def main():
         torch.cuda.set_device(local)
         r = decode_measure(rb, torch, torch.device("cuda", local), decode_batches(args), new_tokens=args.decode_new)
         print(json.dumps({"decode": r}), flush=True)
+        return 0
+    if args.stream_model_only:
+        import torch
+        import riallm_b200 as rb
+        torch.cuda.set_device(local)
+        r = stream_model_measure(rb, torch, torch.device("cuda", local))
+        print(json.dumps({"streaming_model": r}), flush=True)
         return 0
     if args.quant_only or args.fine_grained_only:
         import torch

@@ -286,8 +286,66 @@ typedef enum riallm_phase {
   RIALLM_PHASE_DOWN = 3,     /* expert down GEMM */
   RIALLM_PHASE_SHARED = 4,   /* shared expert */
   RIALLM_PHASE_COMBINE = 5,  /* weighted combine */
-  RIALLM_NUM_PHASES = 6
+  RIALLM_PHASE_DISPATCH = 6, /* expert parallel: token rows to the experts' ranks */
+  RIALLM_PHASE_RETURN = 7,   /* expert parallel: expert outputs back to the tokens' ranks */
+  RIALLM_NUM_PHASES = 8
 } riallm_phase;
+
+/* ------------------------------------------------ expert parallelism
+ * No counterpart in the reference (riallm runs every layer on one device,
+ * src/model.rs:231-258). Ranks of one node, one context per GPU: rank r of
+ * W owns experts [r E/W, (r+1) E/W). The library opens NCCL at run time
+ * (libnccl.so.2) and keeps one communicator per context. */
+
+/* A fresh 128-byte NCCL unique id (ncclUniqueId); rank 0 makes it and the
+ * caller hands it to every rank over its own channel.
+ * RIALLM_ERR_CONFIG if NCCL cannot be loaded. */
+int32_t riallm_cuda_ep_unique_id(uint8_t* unique_id_out);
+/* Joins the W ranks' communicator (collective: every rank calls it with the
+ * same id). */
+int32_t riallm_cuda_ep_init(riallm_ctx* ctx, const uint8_t* unique_id, int32_t rank, int32_t world);
+/* Leaves it (also done by riallm_cuda_ctx_destroy). */
+int32_t riallm_cuda_ep_destroy(riallm_ctx* ctx);
+/* RIALLM_OK, or RIALLM_ERR_CUDA with the message when NCCL reports an
+ * asynchronous error on the communicator (a peer died or a link failed):
+ * a host watchdog polls it between steps. */
+int32_t riallm_cuda_ep_async_error(riallm_ctx* ctx);
+
+/* The expert-parallel MoE block (apply_qwen3_5_moe, src/model.rs:751-818,
+ * split over the ranks): x and out are this rank's [T, H] bf16 tokens;
+ * w->gate is the full router [E, H], w->gate_up_proj / w->down_proj hold
+ * only this rank's experts ([E/W, 2I, H], [E/W, H, I];
+ * QuantizedTensor::expert_slice). Every rank calls it with the same T >= 1
+ * and shape. Each rank routes its own tokens over all E experts, sends the
+ * token rows of every pair to the rank owning the pair's expert (NCCL
+ * point-to-point, one message per rank and expert), runs its experts on
+ * what it received, sends the outputs back, and sums each token's pairs in
+ * expert-ascending order with the routing weights, as riallm_cuda_moe_forward
+ * does (outputs equal up to float32 summation order inside the expert
+ * GEMMs). The exchange sizes are copied to the host once per call (a
+ * synchronization of `stream`), so a call cannot be captured in a CUDA
+ * graph. Routed experts only. */
+int32_t riallm_cuda_moe_forward_ep_a2a(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x,
+                                       void* out, int32_t T, int32_t H, int32_t I, int32_t E, int32_t k,
+                                       uint32_t flags, void* stream);
+
+/* Host-only helper of the exchange above (no device work): from the pair
+ * counts each rank sends to this rank, recv_counts[s * e_local + e] (rank s,
+ * local expert e), where the received rows go: expert_counts[e],
+ * expert_offsets[e] (e_local + 1 entries, expert-major) and
+ * block_pos[s * e_local + e] (first row of rank s's rows for expert e). */
+int32_t riallm_ep_exchange_plan(int32_t world, int32_t e_local, const int32_t* recv_counts,
+                                int32_t* expert_counts, int32_t* expert_offsets, int32_t* block_pos);
+
+/* ------------------------------------------------------------ events
+ * Ordering between the caller's streams (riallm has no streams; its device
+ * work is synchronous). Events are created without timing. */
+int32_t riallm_cuda_event_create(riallm_ctx* ctx, void** event_out);
+int32_t riallm_cuda_event_destroy(riallm_ctx* ctx, void* event);
+int32_t riallm_cuda_event_record(riallm_ctx* ctx, void* event, void* stream);
+/* Makes `stream` wait for the event's last record (no host blocking). */
+int32_t riallm_cuda_stream_wait_event(riallm_ctx* ctx, void* stream, void* event);
+int32_t riallm_cuda_event_synchronize(riallm_ctx* ctx, void* event);
 
 /* ---------------------------------------------------------- decoder layer
  * The dense parts of a decoder layer around the MoE block, for end-to-end
@@ -321,7 +379,7 @@ int32_t riallm_cuda_rope_kv_append(riallm_ctx* ctx, const void* qkv, const int32
  * src/model.rs:1317-1328): row b*T + t attends cache positions
  * [0, pos[b] + t] (clamped to S_max) with scores q.k / sqrt(d), a softmax
  * and the weighted sum of v, all float32. q and out are [B*T, nh*d].
- * d is 64 or 128; nh / nkv is 1, 2, 4 or 8. When the (sequence, kv head,
+ * d is 64 or 128; nh / nkv is 1, 2, 4, 6 or 8. When the (sequence, kv head,
  * token) groups are too few to fill the GPU, each group's keys are split
  * over several CTAs that merge through a workspace owned by the context:
  * calls of one context must not overlap (issue them on one stream). */

@@ -100,6 +100,18 @@ SIGNATURES = {
     "riallm_cuda_memcpy_d2h_async": (_i32, [_vp, _vp, _vp, _u64, _vp]),
     "riallm_cuda_stream_synchronize": (_i32, [_vp, _vp]),
     "riallm_cuda_ctx_set_wait_limit": (_i32, [_vp, _u64]),
+    "riallm_cuda_ep_unique_id": (_i32, [_vp]),
+    "riallm_cuda_ep_init": (_i32, [_vp, _vp, _i32, _i32]),
+    "riallm_cuda_ep_destroy": (_i32, [_vp]),
+    "riallm_cuda_ep_async_error": (_i32, [_vp]),
+    "riallm_cuda_moe_forward_ep_a2a": (_i32, [_vp, ctypes.POINTER(CMoeWeights), _vp, _vp, _i32, _i32, _i32,
+                                              _i32, _i32, _u32, _vp]),
+    "riallm_ep_exchange_plan": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp]),
+    "riallm_cuda_event_create": (_i32, [_vp, _pp]),
+    "riallm_cuda_event_destroy": (_i32, [_vp, _vp]),
+    "riallm_cuda_event_record": (_i32, [_vp, _vp, _vp]),
+    "riallm_cuda_stream_wait_event": (_i32, [_vp, _vp, _vp]),
+    "riallm_cuda_event_synchronize": (_i32, [_vp, _vp]),
     "riallm_cuda_ctx_expire_next_wait": (_i32, [_vp]),
     "riallm_cuda_memory_stats": (_i32, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
     "riallm_quant_num_blocks": (_u64, [_i32, _u64]),
@@ -133,7 +145,7 @@ SIGNATURES = {
     "riallm_cuda_linear_bf16": (_i32, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp]),
 }
 
-PHASES = ("route", "gather", "gate_up", "down", "shared", "combine")
+PHASES = ("route", "gather", "gate_up", "down", "shared", "combine", "dispatch", "return")
 
 _lib: Optional[ctypes.CDLL] = None
 

@@ -19,7 +19,7 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libriallm_cuda.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
-SOURCES = ["api.cu", "quant.cu", "route.cu", "expert_tc.cu", "noalloc.cu", "stream.cu", "decoder.cu"]
+SOURCES = ["api.cu", "quant.cu", "route.cu", "expert_tc.cu", "noalloc.cu", "stream.cu", "decoder.cu", "ep.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 
 NVCC_FLAGS = [
@@ -63,7 +63,7 @@ def build(verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), SOURCES))
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB, *objs]
+        cmd = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB, *objs, "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -92,37 +92,6 @@ int set_device(riallm_ctx* ctx) {
   return RIALLM_OK;
 }
 
-// Phase profiling: an event pair per phase per call when enabled.
-cudaEvent_t take_event(riallm_ctx* ctx) {
-  if (!ctx->event_pool.empty()) {
-    cudaEvent_t e = ctx->event_pool.back();
-    ctx->event_pool.pop_back();
-    return e;
-  }
-  cudaEvent_t e = nullptr;
-  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
-  return e;
-}
-
-struct PhaseScope {
-  riallm_ctx* ctx;
-  cudaStream_t st;
-  int phase;
-  cudaEvent_t start = nullptr;
-  PhaseScope(riallm_ctx* c, cudaStream_t s, int p) : ctx(c), st(s), phase(p) {
-    if (ctx->profiling && (start = take_event(ctx))) cudaEventRecord(start, st);
-  }
-  ~PhaseScope() {
-    if (!start) return;
-    cudaEvent_t stop = take_event(ctx);
-    if (!stop) {
-      ctx->event_pool.push_back(start);
-      return;
-    }
-    cudaEventRecord(stop, st);
-    ctx->pending.push_back({phase, start, stop});
-  }
-};
 
 }  // namespace
 
@@ -234,6 +203,7 @@ int32_t riallm_cuda_ctx_create(int32_t device, riallm_ctx** out) {
 
 int32_t riallm_cuda_ctx_destroy(riallm_ctx* ctx) {
   if (!ctx) return RIALLM_ERR_INVALID;
+  riallm_cuda_ep_destroy(ctx);
   cudaSetDevice(ctx->device);
   if (ctx->arena) cudaFree(ctx->arena);
   for (void* a : ctx->retired_arenas) cudaFree(a);
@@ -405,6 +375,8 @@ static int route_into(riallm_ctx* ctx, const riallm_qtensor& gate, const void* x
   a.inv_pos = (int*)(base + L.inv_pos);
   a.done = (unsigned*)(base + L.sync);
   a.cta_base = (int*)(base + L.cta_base);
+  if ((int64_t)T * k > rl::kSortOneCta)
+    RL_CUDA(ctx, cudaMemsetAsync(a.cta_base, 0, rl::router_cta_bytes(T, H, E), st), "router group counts");
   RL_CUDA(ctx, rl::launch_router(a, gate.qtype, st), "router");
   return RIALLM_OK;
 }
@@ -475,14 +447,14 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
   cudaStream_t st = (cudaStream_t)stream;
 
   {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_ROUTE);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_ROUTE);
     if (int s = route_into(ctx, w->gate, x, T, H, E, k, bf16, base, L, st)) return s;
     ctx->launches += 1;
   }
   const int* counts = (const int*)(base + L.counts);
   const int* offsets = (const int*)(base + L.offsets);
   {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_GATHER);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_GATHER);
     RL_CUDA(ctx, rl::launch_gather(x, bf16, (const int*)(base + L.perm_pair), k, P, H, base + L.x_perm,
                                    bf16 && w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st),
             "gather");
@@ -540,12 +512,12 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
       ctx->expire_next_wait = false;
     }
     {
-      PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
+      rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_GATE_UP);
       RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
       ctx->launches += 1;
     }
     {
-      PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
+      rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_DOWN);
       RL_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");
       ctx->launches += 1;
     }
@@ -568,7 +540,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     g.P = P;
     g.round_w_bf16 = false;
     {
-      PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
+      rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_GATE_UP);
       RL_CUDA(ctx, rl::launch_grouped_f32(g, st), "expert gate_up (f32)");
       RL_CUDA(ctx, rl::launch_swiglu(proj, 2 * I, proj + I, 2 * I, base + L.h_perm, I, P, I, false, st),
               "swiglu");
@@ -583,7 +555,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
     d.y = (float*)(base + L.y_perm);
     d.ldy = H;
     {
-      PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
+      rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_DOWN);
       RL_CUDA(ctx, rl::launch_grouped_f32(d, st), "expert down (f32)");
       ctx->launches += 1;
     }
@@ -592,7 +564,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
   const float* shared_y = nullptr;
   const float* shared_gate = nullptr;
   if (shared) {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_SHARED);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_SHARED);
     ctx->launches += 5;
     rl::GroupedF32Args s{};
     s.K = H;
@@ -637,7 +609,7 @@ int32_t riallm_cuda_moe_forward(riallm_ctx* ctx, const riallm_moe_weights* w, co
   }
 
   {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_COMBINE);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_COMBINE);
     RL_CUDA(ctx, rl::launch_combine((const float*)(base + L.y_perm), (const int*)(base + L.inv_pos),
                                     (const int*)(base + L.topk_idx), (const float*)(base + L.topk_w), T, k, H,
                                     shared_y, shared_gate, out, bf16, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st,
@@ -672,7 +644,7 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
   char* base = (char*)ctx->arena;
   cudaStream_t st = (cudaStream_t)stream;
   {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_ROUTE);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_ROUTE);
     if (int s = route_into(ctx, w->gate, x, T, H, E, k, true, base, L, st)) return s;
     ctx->launches += 1;
   }
@@ -680,7 +652,7 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
   const int* counts = (const int*)(base + L.counts) + e_begin;
   const int* offsets = (const int*)(base + L.offsets) + e_begin;
   {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_GATHER);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_GATHER);
     RL_CUDA(ctx, rl::launch_gather(x, true, (const int*)(base + L.perm_pair), k, P, H, base + L.x_perm,
                                    w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st, offsets,
                                    offsets + e_local),
@@ -710,7 +682,7 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
   g.pdl = true;  // follows the gather
   g.flag_wait_ns = ctx->flag_wait_ns;
   {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_GATE_UP);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_GATE_UP);
     RL_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
     ctx->launches += 1;
   }
@@ -729,12 +701,12 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
   d.ld_out = H;
   d.pdl = true;  // follows the gate_up GEMM
   {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_DOWN);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_DOWN);
     RL_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");
     ctx->launches += 1;
   }
   {
-    PhaseScope ps(ctx, st, RIALLM_PHASE_COMBINE);
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_COMBINE);
     RL_CUDA(ctx, rl::launch_combine((const float*)(base + L.y_perm), (const int*)(base + L.inv_pos),
                                     (const int*)(base + L.topk_idx), (const float*)(base + L.topk_w), T, k, H,
                                     nullptr, nullptr, partial, false, false, st, e_begin, e_begin + e_local,
@@ -743,6 +715,80 @@ int32_t riallm_cuda_moe_forward_ep(riallm_ctx* ctx, const riallm_moe_weights* w,
     ctx->launches += 1;
   }
   if (ctx->profiling) ctx->profiled_calls += 1;
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_moe_forward_ep_a2a(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x, void* out,
+                                       int32_t T, int32_t H, int32_t I, int32_t E, int32_t k, uint32_t flags,
+                                       void* stream) {
+  if (!ctx || !w) return RIALLM_ERR_INVALID;
+  if (!ctx->ep_comm) return set_err(ctx, RIALLM_ERR_CONFIG, "riallm_cuda_ep_init was not called on this context");
+  if (T < 1) return set_err(ctx, RIALLM_ERR_CONFIG, "every rank calls with the same T >= 1");
+  if (!x || !out) return set_err(ctx, RIALLM_ERR_INVALID, "null x/out");
+  if (int s = check_shapes(ctx, T, H, I, E, k)) return s;
+  const int W = ctx->ep_world;
+  if (E % W) return set_err(ctx, RIALLM_ERR_CONFIG, "experts do not split evenly over the ranks");
+  const int EL = E / W;
+  if (w->shared_gate_proj.data != nullptr)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "expert-parallel calls take routed experts only");
+  if (int s = check_qtensor(ctx, w->gate, (uint64_t)E * H, "mlp.gate.weight", false)) return s;
+  if (int s = check_qtensor(ctx, w->gate_up_proj, (uint64_t)EL * 2 * I * H, "mlp.experts.gate_up_proj", true))
+    return s;
+  if (int s = check_qtensor(ctx, w->down_proj, (uint64_t)EL * H * I, "mlp.experts.down_proj", true)) return s;
+  if (!aligned16(x) || !aligned16(out)) return set_err(ctx, RIALLM_ERR_INVALID, "x/out must be 16-byte aligned");
+  if (int s = set_device(ctx)) return s;
+  const int P = T * k;
+  MoeLayout L = rl::moe_layout(T, H, I, E, k, RIALLM_DTYPE_BF16, 0, ctx->num_sms);
+  if (int s = ensure_arena(ctx, L.total + rl_ep_extra_bytes(T, H, I, E, k, W, ctx->num_sms))) return s;
+  char* base = (char*)ctx->arena;
+  cudaStream_t st = (cudaStream_t)stream;
+  {
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_ROUTE);
+    if (int s = route_into(ctx, w->gate, x, T, H, E, k, true, base, L, st)) return s;
+    ctx->launches += 1;
+  }
+  {
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_GATHER);
+    RL_CUDA(ctx, rl::launch_gather(x, true, (const int*)(base + L.perm_pair), k, P, H, base + L.x_perm,
+                                   w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st),
+            "gather");
+    ctx->launches += 1;
+  }
+  if (int s = rl_ep_forward(ctx, w, x, out, T, H, I, E, k, flags, st, base, L, L.total)) return s;
+  if (ctx->profiling) ctx->profiled_calls += 1;
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_event_create(riallm_ctx* ctx, void** event_out) {
+  if (!ctx || !event_out) return RIALLM_ERR_INVALID;
+  if (int s = set_device(ctx)) return s;
+  cudaEvent_t e = nullptr;
+  RL_CUDA(ctx, cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "cudaEventCreate");
+  *event_out = e;
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_event_destroy(riallm_ctx* ctx, void* event) {
+  if (!ctx || !event) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaEventDestroy((cudaEvent_t)event), "cudaEventDestroy");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_event_record(riallm_ctx* ctx, void* event, void* stream) {
+  if (!ctx || !event) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream), "cudaEventRecord");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_stream_wait_event(riallm_ctx* ctx, void* stream, void* event) {
+  if (!ctx || !event) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0), "cudaStreamWaitEvent");
+  return RIALLM_OK;
+}
+
+int32_t riallm_cuda_event_synchronize(riallm_ctx* ctx, void* event) {
+  if (!ctx || !event) return RIALLM_ERR_INVALID;
+  RL_CUDA(ctx, cudaEventSynchronize((cudaEvent_t)event), "cudaEventSynchronize");
   return RIALLM_OK;
 }
 

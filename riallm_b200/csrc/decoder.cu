@@ -385,6 +385,7 @@ cudaError_t launch_attention_d(int rep, dim3 grid, const uint16_t* q, const uint
     RL_ATTN_CASE(1)
     RL_ATTN_CASE(2)
     RL_ATTN_CASE(4)
+    RL_ATTN_CASE(6)
     RL_ATTN_CASE(8)
 #undef RL_ATTN_CASE
     default:
@@ -454,8 +455,8 @@ int32_t riallm_cuda_attention(riallm_ctx* ctx, const void* q, const void* k_cach
     return fail(ctx, RIALLM_ERR_CONFIG, "attention: bad dimensions (heads must be a multiple of kv heads)");
   const int rep = nh / nkv;
   if (d != 64 && d != 128) return fail(ctx, RIALLM_ERR_CONFIG, "attention: head_dim must be 64 or 128");
-  if (rep != 1 && rep != 2 && rep != 4 && rep != 8)
-    return fail(ctx, RIALLM_ERR_CONFIG, "attention: heads / kv heads must be 1, 2, 4 or 8");
+  if (rep != 1 && rep != 2 && rep != 4 && rep != 6 && rep != 8)
+    return fail(ctx, RIALLM_ERR_CONFIG, "attention: heads / kv heads must be 1, 2, 4, 6 or 8");
   if (!al16(k_cache) || !al16(v_cache))
     return fail(ctx, RIALLM_ERR_INVALID, "attention: k and v caches must be 16-byte aligned");
   if (B > 65535 || nkv > 65535) return fail(ctx, RIALLM_ERR_CONFIG, "attention: batch or kv heads too large");

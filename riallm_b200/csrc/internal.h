@@ -44,9 +44,50 @@ struct riallm_ctx {
   // the test hook that makes the next MoE call's such wait expire.
   uint64_t flag_wait_ns = 0;
   bool expire_next_wait = false;
+  // Expert parallelism (riallm_cuda_ep_init): the NCCL communicator of this
+  // context's rank, host staging of one call's exchange sizes, and the
+  // receive-side arena (sized by the rows a call actually receives; grown,
+  // never shrunk, freed with the communicator).
+  void* ep_comm = nullptr;
+  int ep_rank = 0, ep_world = 1;
+  std::vector<int32_t> ep_host, ep_upload;
+  void* ep_arena = nullptr;
+  uint64_t ep_arena_bytes = 0;
 };
 
 namespace rl {
+
+// Phase profiling (riallm_cuda_profile_enable): an event pair around a
+// phase on the call's stream, recorded only while profiling is on.
+inline cudaEvent_t take_event(riallm_ctx* ctx) {
+  if (!ctx->event_pool.empty()) {
+    cudaEvent_t e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+struct PhaseTimer {
+  riallm_ctx* ctx;
+  cudaStream_t st;
+  int phase;
+  cudaEvent_t start = nullptr;
+  PhaseTimer(riallm_ctx* c, cudaStream_t s, int p) : ctx(c), st(s), phase(p) {
+    if (ctx->profiling && (start = take_event(ctx))) cudaEventRecord(start, st);
+  }
+  ~PhaseTimer() {
+    if (!start) return;
+    cudaEvent_t stop = take_event(ctx);
+    if (!stop) {
+      ctx->event_pool.push_back(start);
+      return;
+    }
+    cudaEventRecord(stop, st);
+    ctx->pending.push_back({phase, start, stop});
+  }
+};
 
 // Split-key attention: when the (sequence, kv head, token) groups of a call
 // fill fewer than 2 CTAs per SM, each group's keys are split over several
@@ -100,8 +141,9 @@ struct RouterArgs {
   int* perm_pair;
   int* inv_pos;
   unsigned* done;  // zero between calls; the last CTA resets it
-  // Calls of more than kSortOneCta pairs: per router CTA and expert, the
-  // CTA's pair count, then the base of its pairs (router_cta_bytes()).
+  // Calls of more than kSortOneCta pairs: per group of kSortGroup tokens
+  // and expert, the group's pair count (zeroed before the router runs),
+  // then the base of its pairs (router_cta_bytes()).
   int* cta_base;
 };
 // Pairs (T * k) up to which the router's last CTA sorts all pairs by itself;
@@ -110,9 +152,10 @@ constexpr int64_t kSortOneCta = 16384;
 constexpr int kMaxExperts = 256;
 // Tokens per router CTA (1 for decode-sized calls).
 int router_tile_tokens(int T, int H);
+constexpr int kSortGroup = 64;  // tokens per group of the multi-CTA sort (a multiple of every tile)
 inline uint64_t router_cta_bytes(int T, int H, int E) {
-  const int tt = router_tile_tokens(T, H);
-  return (uint64_t)((T + tt - 1) / tt) * E * 4;
+  (void)H;
+  return (uint64_t)((T + kSortGroup - 1) / kSortGroup) * E * 4;
 }
 cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stream);
 // Gathers token rows into expert-sorted pair order. pair_perm (bf16 only)
@@ -210,3 +253,14 @@ CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, const
                               uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle);
 
 }  // namespace rl
+
+// Expert-parallel block with the token all-to-all (ep.cu): the receive-side
+// scratch that follows a call's regular layout, and the call's exchange,
+// expert GEMMs and combine after routing and gathering (ep_off = where the
+// receive side starts in the arena).
+uint64_t rl_ep_extra_bytes(int T, int H, int I, int E, int k, int W, int num_sms);
+int rl_ep_forward(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x, void* out, int T, int H, int I,
+                  int E, int k, uint32_t flags, cudaStream_t st, char* base, const rl::MoeLayout& L,
+                  uint64_t ep_off);
+int rl_ep_plan(int world, int e_local, const int32_t* recv_counts, int32_t* expert_counts,
+               int32_t* expert_offsets, int32_t* block_pos);

@@ -173,23 +173,36 @@ class Decoder:
     KV cache of `max_seq` positions per sequence."""
 
     def __init__(self, cfg: DecoderConfig, qweights: Dict[str, object], max_batch: int = 1,
-                 max_seq: int = 2048, device: int = 0, streamer=None):
+                 max_seq: int = 2048, device: int = 0, streamer=None, ep=None):
         """streamer: a LayerStreamer over the layers' MoE tensors (router
         gate and experts, one PackedLayer per layer, in layer order); they
         are then not taken from qweights but copied from pinned host memory
         into the streamer's device slots ahead of each layer on every forward
         (ModelOptions.prefetch_layers). Such a decoder runs its decode steps
-        eagerly (the copies are host-driven, so there is no decode graph)."""
+        eagerly (the copies are host-driven, so there is no decode graph).
+
+        ep: an ExpertParallelMoE handle (riallm_b200.ep; one process per GPU,
+        every rank running its own batch of sequences through its own
+        Decoder in lockstep). qweights then holds this rank's experts of
+        every layer (QuantizedTensor.expert_slice) and the full router; the
+        attention, norms, embedding and LM head are replicated. Each MoE
+        block all-gathers the ranks' tokens, runs the local experts and
+        reduce-scatters the partial sums (NCCL collectives, which the decode
+        graph captures)."""
+        if streamer is not None and ep is not None:
+            raise ConfigError("layer streaming and expert parallelism do not combine")
         c = self.cfg = cfg
-        if c.heads % c.kv_heads or c.heads // c.kv_heads not in (1, 2, 4, 8) or c.head_dim not in (64, 128):
-            raise ConfigError("need heads / kv_heads in {1, 2, 4, 8} and head_dim 64 or 128")
+        if c.heads % c.kv_heads or c.heads // c.kv_heads not in (1, 2, 4, 6, 8) or c.head_dim not in (64, 128):
+            raise ConfigError("need heads / kv_heads in {1, 2, 4, 6, 8} and head_dim 64 or 128")
         self.dev = torch.device("cuda", device)
         # Two contexts of its own: prefill calls grow `ctx`'s MoE scratch
         # arena as needed, while the decode graphs use `ctx_step`, reserved
         # once for max_batch tokens, whose arena therefore never moves.
         self.ctx = Context(device)
         self.ctx_step = Context(device)
-        self.ctx_step.reserve(max_batch, c.hidden, c.intermediate, c.experts, c.top_k, torch.bfloat16)
+        self.ep = ep
+        step_tokens = max_batch * (ep.world if ep is not None else 1)
+        self.ctx_step.reserve(step_tokens, c.hidden, c.intermediate, c.experts, c.top_k, torch.bfloat16)
         self.embed = _bf16(qweights["model.embed_tokens.weight"])
         self.lm_head = _bf16(qweights["lm_head.weight"])
         self.final_norm = qweights["model.norm.weight"].float().contiguous()
@@ -277,7 +290,10 @@ class Decoder:
             if experts_used is not None:
                 counts = route(moe["mlp.gate.weight"], n, c.top_k, c.experts, ctx=moe_ctx)[2]
                 experts_used.append(int((counts > 0).sum().item()))
-            apply_moe(moe, n, c.top_k, c.experts, out=h, add_to_out=True, ctx=moe_ctx)
+            if self.ep is not None:
+                self.ep.forward(n, tensors=moe, add_to=h, ctx=moe_ctx)
+            else:
+                apply_moe(moe, n, c.top_k, c.experts, out=h, add_to_out=True, ctx=moe_ctx)
             if st is not None:
                 st.release(i)
                 st.prefetch(i + st.depth)

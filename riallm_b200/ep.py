@@ -101,7 +101,7 @@ class ExpertParallelMoE:
     output.
     """
 
-    def __init__(self, tensors: Mapping[str, TensorLike], num_experts: int, top_k: int,
+    def __init__(self, tensors: Optional[Mapping[str, TensorLike]], num_experts: int, top_k: int,
                  group: Optional[dist.ProcessGroup] = None, ops: Optional[PartialFn] = None,
                  watch: Optional[PeerWatch] = None):
         self.group = group
@@ -111,27 +111,36 @@ class ExpertParallelMoE:
         self.k = int(top_k)
         self.e_begin, self.e_local = expert_range(self.E, self.rank, self.world)
         self.tensors = tensors
-        self.ops = ops or self._gpu_partial
+        self.ops = ops
         # gloo has no reduce-scatter: it all-reduces and keeps its own slice.
         self.backend = dist.get_backend(group)
         self.watch = watch
 
-    def _gpu_partial(self, x_all: torch.Tensor, e_begin: int, e_local: int) -> torch.Tensor:
-        return apply_moe_ep_partial(self.tensors, x_all, self.k, self.E, e_begin, e_local)
-
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, tensors: Optional[Mapping[str, TensorLike]] = None,
+                add_to: Optional[torch.Tensor] = None, ctx=None) -> torch.Tensor:
+        """x: this rank's tokens [T,H]. tensors: this call's weights (default:
+        the ones given at construction), so one handle serves every layer of
+        a model. With add_to (a [T,H] tensor of x's dtype), the block output
+        is added to it in float32 and rounded once, in place (what
+        apply_moe(..., add_to_out=True) does on one GPU), and add_to is
+        returned. ctx: the library context of the expert kernels."""
         if self.watch is not None:
             self.watch.step()
+        tensors = self.tensors if tensors is None else tensors
         try:
-            return self._forward(x)
+            y = self._forward(x, tensors, ctx)
         except RiallmError:
             raise
         except RuntimeError as exc:
             # A collective that failed or timed out (a peer left during the
             # step, or the process group's timeout expired).
             raise RankFailureError(f"expert-parallel collective failed: {exc}") from exc
+        if add_to is not None:
+            add_to.copy_(add_to.float().add_(y))
+            return add_to
+        return y.to(x.dtype)
 
-    def _forward(self, x: torch.Tensor) -> torch.Tensor:
+    def _forward(self, x: torch.Tensor, tensors, ctx) -> torch.Tensor:
         T, H = x.shape
         W = self.world
         x = x.contiguous()
@@ -142,13 +151,84 @@ class ExpertParallelMoE:
             x_all = torch.cat(parts, 0)
         else:
             dist.all_gather_into_tensor(x_all, x, group=self.group)
-        partial = self.ops(x_all, self.e_begin, self.e_local)
+        if self.ops is not None:
+            partial = self.ops(x_all, self.e_begin, self.e_local)
+        else:
+            partial = apply_moe_ep_partial(tensors, x_all, self.k, self.E, self.e_begin, self.e_local, ctx=ctx)
         if self.backend == "gloo":
             dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
             out = partial[self.rank * T:(self.rank + 1) * T]
         else:
             out = torch.empty((T, H), dtype=partial.dtype, device=partial.device)
             dist.reduce_scatter_tensor(out, partial, op=dist.ReduceOp.SUM, group=self.group)
-        return out.to(x.dtype)
+        return out
 
     __call__ = forward
+
+
+class ExpertParallelA2A:
+    """One rank's expert-parallel MoE block with the token all-to-all inside
+    the library (riallm_cuda_ep_init + riallm_cuda_moe_forward_ep_a2a).
+
+    tensors: the full router "mlp.gate.weight" [E,H] and this rank's experts'
+    "mlp.experts.gate_up_proj" / "mlp.experts.down_proj" (expert_slice of the
+    full tensors, experts [r E/W, (r+1) E/W)). Rank 0 makes the NCCL id and
+    the process group carries it to the other ranks; the library then builds
+    its own communicator on a context of its own. forward(x) takes this
+    rank's bf16 tokens [T,H] (the same T on every rank) and returns their
+    block output. A PeerWatch, when given, checks the peers on the host
+    before every step, and the communicator's asynchronous error state is
+    polled after it: a failed or vanished peer raises RankFailureError."""
+
+    def __init__(self, tensors: Mapping[str, TensorLike], num_experts: int, top_k: int,
+                 group: Optional[dist.ProcessGroup] = None, device: Optional[int] = None,
+                 watch: Optional[PeerWatch] = None):
+        import ctypes
+        from . import Context, lib
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.E, self.k = int(num_experts), int(top_k)
+        self.e_begin, self.e_local = expert_range(self.E, self.rank, self.world)
+        self.tensors = tensors
+        self.watch = watch
+        dev = torch.cuda.current_device() if device is None else int(device)
+        self.ctx = Context(dev)
+        buf = (ctypes.c_uint8 * 128)()
+        if self.rank == 0:
+            self.ctx.check(lib().riallm_cuda_ep_unique_id(buf))
+        obj = [bytes(buf)]
+        dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        uid = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
+        self.ctx.check(lib().riallm_cuda_ep_init(self.ctx.ptr, uid, self.rank, self.world))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        import ctypes
+        from . import _stream_ptr, _weights, lib
+        if self.watch is not None:
+            self.watch.step()
+        if x.dtype != torch.bfloat16 or not x.is_cuda:
+            raise ConfigError("expert-parallel calls take bf16 CUDA tokens")
+        x = x.contiguous()
+        T, H = x.shape
+        w, keep, gu = _weights(self.tensors)
+        I = int(gu.shape[1]) // 2
+        out = torch.empty_like(x)
+        self.ctx.check(lib().riallm_cuda_moe_forward_ep_a2a(self.ctx.ptr, ctypes.byref(w), x.data_ptr(),
+                                                            out.data_ptr(), T, H, I, self.E, self.k, 0,
+                                                            _stream_ptr(x)))
+        rc = lib().riallm_cuda_ep_async_error(self.ctx.ptr)
+        if rc != 0:
+            raise RankFailureError(lib().riallm_cuda_last_error(self.ctx.ptr).decode())
+        del keep
+        return out
+
+    __call__ = forward
+
+    def close(self):
+        from . import lib
+        if self.ctx is not None:
+            torch.cuda.synchronize()
+            lib().riallm_cuda_ep_destroy(self.ctx.ptr)
+            self.ctx.close()
+            self.ctx = None

@@ -144,3 +144,20 @@ def test_rank_that_leaves_is_reported(tmp_path, use_watch):
     assert msg.startswith("RankFailureError"), msg
     if use_watch:
         assert "ranks=[1]" in msg, msg
+
+
+def test_exchange_plan_places_rows_expert_major(rb):
+    """riallm_ep_exchange_plan (host-only): rows received from every rank
+    land expert-major, ranks ascending inside an expert."""
+    import ctypes
+    L = rb.lib()
+    W, EL = 3, 2
+    rc = np.array([[2, 0], [1, 3], [0, 4]], np.int32)  # [source rank][local expert]
+    cnt = np.zeros(EL, np.int32)
+    off = np.zeros(EL + 1, np.int32)
+    pos = np.zeros((W, EL), np.int32)
+    p = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    assert L.riallm_ep_exchange_plan(W, EL, p(rc), p(cnt), p(off), p(pos)) == 0
+    assert cnt.tolist() == [3, 7] and off.tolist() == [0, 3, 10]
+    assert pos.tolist() == [[0, 3], [2, 3], [3, 6]]
+    assert L.riallm_ep_exchange_plan(0, EL, p(rc), p(cnt), p(off), p(pos)) != 0

@@ -115,7 +115,7 @@ def test_configured_tiny_model_greedy_tokens(rb, oracle_lib):
     for row in report:
         print("%d %d %d %.3e %.3e" % row)
     print(f"identical greedy tokens: {same}/16")
-    assert same >= 14
+    assert same == 16, "the configured model must reproduce the oracle's greedy tokens"
     model.close()
 
 

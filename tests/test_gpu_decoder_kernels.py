@@ -59,7 +59,8 @@ def _ref_attention(q, kc, vc, pos, T, nh, nkv, d):
 SHAPES = [(3, 4, [0, 9, 600]), (2, 80, [0, 300])]
 
 
-@pytest.mark.parametrize("nh,nkv,d,shape", [(8, 2, 128, 0), (4, 4, 64, 0), (16, 2, 64, 0), (8, 2, 128, 1)])
+@pytest.mark.parametrize("nh,nkv,d,shape", [(8, 2, 128, 0), (4, 4, 64, 0), (16, 2, 64, 0), (8, 2, 128, 1),
+                                                (48, 8, 128, 0)])
 def test_rope_append_and_attention(rb, nh, nkv, d, shape):
     from riallm_b200 import Context, lib
     from riallm_b200.decoder import apply_rope, rope_tables, inv_freq
@@ -108,7 +109,7 @@ def test_argument_errors(rb):
     q = torch.zeros(2, 6 * 128, dtype=torch.bfloat16, device="cuda")
     kc = torch.zeros(1, 2, 8, 128, dtype=torch.bfloat16, device="cuda")
     pos = torch.zeros(1, dtype=torch.int32, device="cuda")
-    with pytest.raises(ConfigError, match="1, 2, 4 or 8"):  # 6 heads over 2 kv heads = 3
+    with pytest.raises(ConfigError, match="1, 2, 4, 6 or 8"):  # 6 heads over 2 kv heads = 3
         ctx.check(lib().riallm_cuda_attention(ctx.ptr, q.data_ptr(), kc.data_ptr(), kc.data_ptr(), pos.data_ptr(),
                                               1, 2, 6, 2, 128, 8, q.data_ptr(), st))
 
