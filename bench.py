@@ -516,17 +516,26 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
                "mlp.experts.down_proj": d["mlp.experts.down_proj"].expert_slice(e_b, e_l)}
     gen = torch.Generator(device=device).manual_seed(1000 + args.tokens + 7919 * rank)
     x = torch.empty(args.tokens, H, device=device).normal_(0, 1, generator=gen).to(torch.bfloat16)
-    ctx_rep = rb.Context(device.index or 0)
-    ctx_rep.reserve(world * args.tokens, H, I, E, TOP_K, torch.bfloat16)
-    rep = ExpertParallelMoE(local_w, E, TOP_K)
-    a2a = ExpertParallelA2A(local_w, E, TOP_K, device=local)
-    paths = {"replicated": (lambda v: rep(v, ctx=ctx_rep), ctx_rep),
-             "all_to_all": (a2a, a2a.ctx)}
+    made = {}
+
+    def make(name):
+        # Built in the order timed, on every rank alike: the all-to-all
+        # handle brings its own NCCL communicator, which need not exist
+        # while the other design is timed.
+        if name == "replicated":
+            ctx_rep = rb.Context(device.index or 0)
+            ctx_rep.reserve(world * args.tokens, H, I, E, TOP_K, torch.bfloat16)
+            rep = ExpertParallelMoE(local_w, E, TOP_K)
+            made[name] = (lambda v: rep(v, ctx=ctx_rep), ctx_rep, ctx_rep.close)
+        else:
+            a2a = ExpertParallelA2A(local_w, E, TOP_K, device=local)
+            made[name] = (a2a, a2a.ctx, a2a.close)
+        return made[name]
     head = args.ep_path
-    order = [head] + ([] if args.no_sweep else [p for p in paths if p != head])
+    order = [head] + ([] if args.no_sweep else [p for p in ("replicated", "all_to_all") if p != head])
     res, clk = {}, None
     for name in order:
-        fn, ctx = paths[name]
+        fn, ctx, _ = make(name)
         fn(x)
         l0 = ctx.launch_count()
         fn(x)
@@ -547,7 +556,7 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     value = res[head]["tokens_per_s"]
     launches_per_step = res[head]["launches_per_step"]
     ep_check = res[head]["check"]
-    blk = paths[head][0]
+    blk = made[head][0]
     ph = res[head]["phase_ms_per_step"]
 
     # Local expert GEMM phases on this rank (roofline of the dominant kernel).
@@ -616,8 +625,8 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     tt = torch.tensor([t0.elapsed_time(t1)], device="cuda")
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     e2e_ms = float(tt.item())
-    a2a.close()
-    ctx_rep.close()
+    for _, _, close in made.values():
+        close()
     fine_ep = None if args.no_sweep else ep_fine_measure(rb, torch, dist, device, rank, world)
     dec_ep = None if args.no_decode else ep_decode_measure(rb, torch, dist, device, rank, world,
                                                            decode_batches(args), new_tokens=min(args.decode_new, 64))
@@ -1046,17 +1055,23 @@ def zipf_bias(torch, n, s=1.1, seed=4):
     return torch.log(w / w.sum()).float()
 
 
-def quant_measure(rb, torch, device, d, hbm_peak, peak_src, reps=5):
+def quant_measure(rb, torch, device, d, hbm_peak, peak_src, reps=5, experts=None):
     """The standalone block dequantizer and quantizer (src/quantization.rs:
     45-245) on the Mixtral-8x7B layer's gate_up_proj (8 x 28672 x 4096 =
     939,524,096 weights): HBM GB/s = algorithmic bytes (codes + float32
     scales and zero points read, values written; or float32 read and codes,
     scales, zero points written) / CUDA-event time on the launching stream,
     best of `reps` launches after one warm-up, against the measured copy
-    peak. Inputs and outputs are larger than L2."""
+    peak. Inputs and outputs are larger than L2. experts=K takes the first K
+    experts' slice only (K = 1: 117 M weights, still above L2 with its
+    output), the size a profiler capture is run on."""
     gu = d["mlp.experts.gate_up_proj"]
+    label = "mixtral8x7b gate_up_proj [8, 28672, 4096]"
+    if experts:
+        gu = gu.expert_slice(0, experts)
+        label = f"mixtral8x7b gate_up_proj, experts 0..{experts - 1} [{experts}, 28672, 4096]"
     n = gu.numel
-    out = {"tensor": "mixtral8x7b gate_up_proj [8, 28672, 4096]", "elements": n,
+    out = {"tensor": label, "elements": n,
            "peak": hbm_peak, "peak_source": peak_src, "runs": []}
 
     def best(fn):
@@ -1203,6 +1218,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-decode", action="store_true", help="skip the Mixtral-8x7B decode measurement")
     ap.add_argument("--quant-only", action="store_true",
                     help="only the standalone quantize / dequantize measurement (prints {\"quant\": ...})")
+    ap.add_argument("--quant-experts", type=int, default=0,
+                    help="with --quant-only: the first K experts' slice of gate_up_proj instead of all 8")
     ap.add_argument("--fine-grained-only", action="store_true",
                     help="only the 128-expert top-8 measurement (prints {\"fine_grained\": ...})")
     ap.add_argument("--stream-model-only", action="store_true",
@@ -1243,7 +1260,8 @@ def main():
         device = torch.device("cuda", local)
         hbm_peak, _, _, peak_src = load_peaks()
         if args.quant_only:
-            r = quant_measure(rb, torch, device, make_layer(rb, torch, device), hbm_peak, peak_src)
+            r = quant_measure(rb, torch, device, make_layer(rb, torch, device), hbm_peak, peak_src,
+                              experts=args.quant_experts or None)
             print(json.dumps({"quant": r}), flush=True)
         else:
             print(json.dumps({"fine_grained": fine_grained_measure(rb, torch, device)}), flush=True)

@@ -318,13 +318,15 @@ int32_t riallm_cuda_ep_async_error(riallm_ctx* ctx);
  * QuantizedTensor::expert_slice). Every rank calls it with the same T >= 1
  * and shape. Each rank routes its own tokens over all E experts, sends the
  * token rows of every pair to the rank owning the pair's expert (NCCL
- * point-to-point, one message per rank and expert), runs its experts on
- * what it received, sends the outputs back, and sums each token's pairs in
+ * point-to-point, one message per peer each way), runs its experts on what
+ * it received, sends the outputs back, and sums each token's pairs in
  * expert-ascending order with the routing weights, as riallm_cuda_moe_forward
  * does (outputs equal up to float32 summation order inside the expert
  * GEMMs). The exchange sizes are copied to the host once per call (a
  * synchronization of `stream`), so a call cannot be captured in a CUDA
- * graph. Routed experts only. */
+ * graph. The receive buffers live in a second arena of the context, sized
+ * by the rows the call receives and grown with cudaMalloc when a call
+ * receives more. Routed experts only. */
 int32_t riallm_cuda_moe_forward_ep_a2a(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x,
                                        void* out, int32_t T, int32_t H, int32_t I, int32_t E, int32_t k,
                                        uint32_t flags, void* stream);

@@ -118,6 +118,8 @@ MoeLayout moe_layout(int T, int H, int I, int E, int k, int act_dtype, int share
   L.perm_pair = take(P * 4);
   L.inv_pos = take(P * 4);
   L.cta_base = take((int64_t)P > kSortOneCta ? router_cta_bytes(T, H, E) : 0);
+  L.gate_f32_bytes = router_tile_tokens(T, H) > 1 ? (uint64_t)E * H * 4 : 0;
+  L.gate_f32 = take(L.gate_f32_bytes);
   L.x_perm = take(P * H * esz);
   L.h_perm = take(P * I * esz);
   L.y_perm = take(P * H * 4);
@@ -377,7 +379,21 @@ static int route_into(riallm_ctx* ctx, const riallm_qtensor& gate, const void* x
   a.cta_base = (int*)(base + L.cta_base);
   if ((int64_t)T * k > rl::kSortOneCta)
     RL_CUDA(ctx, cudaMemsetAsync(a.cta_base, 0, rl::router_cta_bytes(T, H, E), st), "router group counts");
-  RL_CUDA(ctx, rl::launch_router(a, gate.qtype, st), "router");
+  int qtype = gate.qtype;
+  if (qtype != RIALLM_COMPRESSION_NONE && L.gate_f32_bytes) {
+    // Token-tiled calls decode the router weight once (the reference's
+    // decode, src/quantization.rs:45-95, the same float32 values the router
+    // would decode per CTA), so every CTA reads float32 rows: the per-CTA
+    // decode was a third of the router's instructions.
+    float* gf = reinterpret_cast<float*>(base + L.gate_f32);
+    RL_CUDA(ctx, rl::launch_dequant(gate, 0, gf, RIALLM_DTYPE_F32, ctx->num_sms, st), "router weight decode");
+    ctx->launches += 1;
+    a.gdata = gf;
+    a.gscales = a.gzeros = nullptr;
+    a.n_scales = a.n_zeros = 0;
+    qtype = RIALLM_COMPRESSION_NONE;
+  }
+  RL_CUDA(ctx, rl::launch_router(a, qtype, st), "router");
   return RIALLM_OK;
 }
 

@@ -111,6 +111,9 @@ struct MoeLayout {
   uint64_t sync, sk_ws, topk_idx, topk_w, counts, offsets, perm_pair, inv_pos;
   uint64_t x_perm, h_perm, y_perm, proj;
   uint64_t cta_base;  // router per-CTA pair bases (multi-CTA sort)
+  // Token-tiled router calls: the quantized router weight decoded once to
+  // float32 [E, H] (0 bytes when the router keeps one token per CTA).
+  uint64_t gate_f32, gate_f32_bytes;
   uint64_t sh_g, sh_u, sh_h, sh_y, sh_gate;
   uint64_t total;
 };

@@ -135,7 +135,7 @@ __device__ __forceinline__ void store8(__nv_bfloat16* out, uint64_t e0, const fl
   *reinterpret_cast<uint4*>(out + e0) = w;
 }
 
-// NF4, 64-element blocks (the format's block size), coalesced: item i of
+// NF4, 64-element blocks (the format's block size), coalesced: thread i of
 // the grid-stride loop decodes elements 8i .. 8i+7 from one 4-byte word of
 // codes, so a warp reads 128 contiguous bytes and writes 1 KiB (float32) or
 // 512 bytes (bf16) contiguous with 16-byte stores. Elements 8i .. 8i+6 use
@@ -143,74 +143,53 @@ __device__ __forceinline__ void store8(__nv_bfloat16* out, uint64_t e0, const fl
 // it is element 63 of its block (src/quantization.rs:55-72). Same arithmetic
 // as dq_value. Requires numel % 8 == 0 and 4-/16-byte aligned data / out.
 template <typename OutT>
-__device__ __forceinline__ void nf4_decode8(const DqParams& p, uint64_t i, uint32_t w, OutT* __restrict__ out) {
-  const uint64_t b0 = i >> 3, b7 = (8 * i + 8) >> 6;
-  const float s0 = b0 < p.n_scales ? __ldg(p.scales + b0) : 1.0f;
-  const float z0 = b0 < p.n_zeros ? __ldg(p.zeros + b0) : 0.0f;
-  const float s7 = b7 < p.n_scales ? __ldg(p.scales + b7) : 1.0f;
-  const float z7 = b7 < p.n_zeros ? __ldg(p.zeros + b7) : 0.0f;
-  float v[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t q = (w >> (4 * j)) & 15u;
-    const float s = j == 7 ? s7 : s0, z = j == 7 ? z7 : z0;
-    if (p.mode == 0) v[j] = __fmul_rn(__fsub_rn((float)q, z), s);
-    else v[j] = __fmul_rn(kNf4Table[q], s);
-  }
-  store8(out, 8 * i, v);
-}
-
-// Each pass of the grid covers one contiguous range of 4 x (grid threads)
-// items, a CTA four consecutive runs of blockDim items of it; a thread
-// issues its four code loads before decoding any. (Four items a whole grid
-// stride apart per thread, i.e. four distant streams per warp, measured
-// slower than one item per thread: 3.56 against 4.45 TB/s.)
-template <typename OutT>
 __global__ void __launch_bounds__(256) dequant_nf4_b64_kernel(DqParams p, OutT* __restrict__ out) {
   const uint64_t nw = p.numel / 8;
   const uint32_t* codes = reinterpret_cast<const uint32_t*>(p.data);
-  const uint64_t bd = blockDim.x, S4 = 4 * (uint64_t)gridDim.x * bd;
-  for (uint64_t base = blockIdx.x * 4 * bd + threadIdx.x; base < nw; base += S4) {
-    uint32_t w[4];
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < nw; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t w = __ldg(codes + i);
+    const uint64_t b0 = i >> 3, b7 = (8 * i + 8) >> 6;
+    const float s0 = b0 < p.n_scales ? __ldg(p.scales + b0) : 1.0f;
+    const float z0 = b0 < p.n_zeros ? __ldg(p.zeros + b0) : 0.0f;
+    const float s7 = b7 < p.n_scales ? __ldg(p.scales + b7) : 1.0f;
+    const float z7 = b7 < p.n_zeros ? __ldg(p.zeros + b7) : 0.0f;
+    float v[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) w[u] = base + u * bd < nw ? __ldg(codes + base + u * bd) : 0u;
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (base + u * bd < nw) nf4_decode8(p, base + u * bd, w[u], out);
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t q = (w >> (4 * j)) & 15u;
+      const float s = j == 7 ? s7 : s0, z = j == 7 ? z7 : z0;
+      if (p.mode == 0) v[j] = __fmul_rn(__fsub_rn((float)q, z), s);
+      else v[j] = __fmul_rn(kNf4Table[q], s);
+    }
+    store8(out, 8 * i, v);
   }
 }
 
-// 8-bit, 128-element blocks, coalesced: item i decodes elements 8i .. 8i+7
-// (one 8-byte load, one block e/128 for all eight); four items per pass as
-// in the NF4 kernel.
-template <typename OutT>
-__device__ __forceinline__ void int8_decode8(const DqParams& p, uint64_t i, uint2 c, OutT* __restrict__ out) {
-  const uint64_t b = i >> 4;
-  const float s = b < p.n_scales ? __ldg(p.scales + b) : 1.0f;
-  const float z = b < p.n_zeros ? __ldg(p.zeros + b) : 0.0f;
-  float v[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float q = (float)(((j < 4 ? c.x : c.y) >> (8 * (j & 3))) & 255u);
-    v[j] = p.mode == 0 ? __fmul_rn(__fsub_rn(q, z), s) : __fadd_rn(__fmul_rn(q, s), z);
-  }
-  store8(out, 8 * i, v);
-}
-
+// 8-bit, 128-element blocks, coalesced: thread i decodes elements 8i .. 8i+7
+// (one 8-byte load, one block e/128 for all eight).
 template <typename OutT>
 __global__ void __launch_bounds__(256) dequant_int8_b128_kernel(DqParams p, OutT* __restrict__ out) {
   const uint64_t nw = p.numel / 8;
   const uint2* codes = reinterpret_cast<const uint2*>(p.data);
-  const uint64_t bd = blockDim.x, S4 = 4 * (uint64_t)gridDim.x * bd;
-  for (uint64_t base = blockIdx.x * 4 * bd + threadIdx.x; base < nw; base += S4) {
-    uint2 c[4];
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < nw; i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint2 c = __ldg(codes + i);
+    const uint64_t b = i >> 4;
+    const float s = b < p.n_scales ? __ldg(p.scales + b) : 1.0f;
+    const float z = b < p.n_zeros ? __ldg(p.zeros + b) : 0.0f;
+    float v[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) c[u] = base + u * bd < nw ? __ldg(codes + base + u * bd) : make_uint2(0u, 0u);
-#pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (base + u * bd < nw) int8_decode8(p, base + u * bd, c[u], out);
+    for (int j = 0; j < 8; ++j) {
+      const float q = (float)(((j < 4 ? c.x : c.y) >> (8 * (j & 3))) & 255u);
+      v[j] = p.mode == 0 ? __fmul_rn(__fsub_rn(q, z), s) : __fadd_rn(__fmul_rn(q, s), z);
+    }
+    store8(out, 8 * i, v);
   }
 }
+
+// (Measured alternatives, both slower on B200 for the 939 M-element Mixtral
+// gate_up tensor: four items per thread a grid stride apart, 3.56 against
+// 4.45 TB/s for NF4 -> bf16; four consecutive blockDim runs per CTA with
+// the four code loads issued first, 3.97 TB/s.)
 
 // --------------------------------------------------------------- quantize
 
@@ -386,7 +365,7 @@ cudaError_t launch_dequant(const riallm_qtensor& t, int mode, void* dst, int dst
   // The format's own block sizes, whole 8-element groups and aligned
   // buffers take the coalesced kernels; anything else the general ones.
   if (t.numel % 8 == 0 && (oa & 15) == 0 && (da & (nf4 ? 3 : 7)) == 0 && t.block_size == (nf4 ? 64 : 128)) {
-    const int g = grid_for((t.numel / 8 + 3) / 4, threads, num_sms);  // four items per thread and pass
+    const int g = grid_for(t.numel / 8, threads, num_sms);
     if (nf4) {
       if (dst_dtype == RIALLM_DTYPE_F32)
         dequant_nf4_b64_kernel<<<g, threads, 0, stream>>>(p, (float*)dst);

@@ -540,42 +540,58 @@ __global__ void combine_kernel(const float* __restrict__ y_perm, const int* __re
                                int k, int H, const float* __restrict__ shared_y,
                                const float* __restrict__ shared_gate, void* out, int out_bf16,
                                int add_to_out, int e_begin, int e_end, int round_w) {
+  // The token's pairs in expert-ascending order (a token's k experts are
+  // distinct, so a pair's rank is the number of its pairs with a smaller
+  // expert), with their y_perm rows and scaled weights, staged once per CTA.
+  __shared__ int s_pos[16];
+  __shared__ float s_w[16];
+  __shared__ int s_n;
   pdl_wait();  // y_perm comes from the down GEMM
   pdl_launch_dependents();
   const int t = blockIdx.x;
-  int ord[16];
-  int exp_id[16];
-  for (int j = 0; j < k; ++j) {
-    exp_id[j] = topk_idx[(uint64_t)t * k + j];
-    ord[j] = j;
-  }
-  for (int a = 1; a < k; ++a) {
-    int v = ord[a];
-    int b = a - 1;
-    while (b >= 0 && exp_id[ord[b]] > exp_id[v]) {
-      ord[b + 1] = ord[b];
-      --b;
+  if (threadIdx.x < 32) {
+    const int j = threadIdx.x;
+    const int e = j < k ? topk_idx[(uint64_t)t * k + j] : 0x7fffffff;
+    // Expert-parallel partial sums keep only this rank's experts.
+    const bool mine = j < k && e >= e_begin && e < e_end;
+    const unsigned keep = __ballot_sync(0xffffffffu, mine);
+    int rank = 0;
+    for (int i = 0; i < k; ++i) {
+      const int ei = __shfl_sync(0xffffffffu, e, i);
+      rank += ((keep >> i) & 1u) && ei < e;
     }
-    ord[b + 1] = v;
-  }
-  float gsig = 0.0f;
-  if (shared_y) gsig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-shared_gate[t])));
-  for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < H; h += gridDim.y * blockDim.x * 4) {
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    for (int jj = 0; jj < k; ++jj) {
-      const int j = ord[jj];
-      // Expert-parallel partial sums keep only this rank's experts.
-      if (exp_id[j] < e_begin || exp_id[j] >= e_end) continue;
-      const int pos = inv_pos[(uint64_t)t * k + j];
+    if (mine) {
+      s_pos[rank] = inv_pos[(uint64_t)t * k + j];
       // src/model.rs:800-802: the weight is cast to the activation dtype
       // (bf16 rounding for bf16 activations) before it scales y.
       const float w0 = topk_w[(uint64_t)t * k + j];
-      const float w = round_w ? __bfloat162float(__float2bfloat16_rn(w0)) : w0;
-      const float4 y = *reinterpret_cast<const float4*>(y_perm + (uint64_t)pos * H + h);
-      a0 = __fadd_rn(a0, __fmul_rn(y.x, w));
-      a1 = __fadd_rn(a1, __fmul_rn(y.y, w));
-      a2 = __fadd_rn(a2, __fmul_rn(y.z, w));
-      a3 = __fadd_rn(a3, __fmul_rn(y.w, w));
+      s_w[rank] = round_w ? __bfloat162float(__float2bfloat16_rn(w0)) : w0;
+    }
+    if (j == 0) s_n = __popc(keep);
+  }
+  __syncthreads();
+  const int n = s_n;
+  float gsig = 0.0f;
+  if (shared_y) gsig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-shared_gate[t])));
+  for (int h = (blockIdx.y * blockDim.x + threadIdx.x) * 4; h < H; h += gridDim.y * blockDim.x * 4) {
+    // Eight rows at a time are loaded before their adds; the adds run in
+    // expert order.
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    for (int j0 = 0; j0 < n; j0 += 8) {
+      float4 y[8];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj)
+        if (j0 + jj < n) y[jj] = *reinterpret_cast<const float4*>(y_perm + (uint64_t)s_pos[j0 + jj] * H + h);
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        if (j0 + jj < n) {
+          const float w = s_w[j0 + jj];
+          a0 = __fadd_rn(a0, __fmul_rn(y[jj].x, w));
+          a1 = __fadd_rn(a1, __fmul_rn(y[jj].y, w));
+          a2 = __fadd_rn(a2, __fmul_rn(y[jj].z, w));
+          a3 = __fadd_rn(a3, __fmul_rn(y[jj].w, w));
+        }
+      }
     }
     if (shared_y) {
       const float4 s = *reinterpret_cast<const float4*>(shared_y + (uint64_t)t * H + h);
