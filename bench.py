@@ -465,6 +465,9 @@ def run_ours(args, rank, world, local):
     streaming_model = None if args.no_stream else stream_model_measure(rb, torch, device)
     decode = None if args.no_decode else decode_measure(rb, torch, device, decode_batches(args),
                                                         new_tokens=args.decode_new)
+    fine_model = None if args.no_decode else decode_measure(
+        rb, torch, device, (1, 64), prompt_len=128, new_tokens=32, seed=4, cfg=fine_model_config(),
+        bytes_per_expert=FINE_BYTES_PER_EXPERT, name="fine-grained")
     fine = None if args.no_sweep else fine_grained_measure(rb, torch, device)
     quant = None if args.no_sweep else quant_measure(rb, torch, device, d, hbm_peak, peak_src)
 
@@ -481,7 +484,7 @@ def run_ours(args, rank, world, local):
             "captured_launches": per_step_launches,
             "clocks": clk.summary(), "sweep": sweep, "streaming": streaming, "streaming_8x22b": streaming_8x22b,
             "streaming_model": streaming_model,
-            "decode": decode, "fine_grained": fine, "quant": quant,
+            "decode": decode, "fine_model_decode": fine_model, "fine_grained": fine, "quant": quant,
         }
         print(json.dumps(line), flush=True)
     del g
@@ -630,6 +633,9 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     fine_ep = None if args.no_sweep else ep_fine_measure(rb, torch, dist, device, rank, world)
     dec_ep = None if args.no_decode else ep_decode_measure(rb, torch, dist, device, rank, world,
                                                            decode_batches(args), new_tokens=min(args.decode_new, 64))
+    fine_dec_ep = None if args.no_decode else ep_decode_measure(
+        rb, torch, dist, device, rank, world, (64,), prompt_len=128, new_tokens=32, seed=4,
+        cfg=fine_model_config(), name="fine-grained")
     nbytes = x.numel() * 2
     e2e = {"value": world * args.tokens * args.steps / (e2e_ms / 1000.0), "unit": "tokens/s",
            "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": nbytes,
@@ -647,13 +653,13 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
             "gpu_launches_note": f"{launches_per_step} library kernels per step per GPU ({head} path) plus its NCCL collectives",
             "clocks": clk.summary(), "sweep": [], "ep_check": ep_check, "ep_path": head, "ep_paths": res,
             "fine_grained_ep": fine_ep,
-            "decode": dec_ep,
+            "decode": dec_ep, "fine_model_decode": fine_dec_ep,
         }
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
     fine_ok = fine_ep is None or all(r["check"]["passed"] for r in fine_ep["runs"])
-    dec_ok = dec_ep is None or all(r["check"]["passed"] for r in dec_ep["runs"] if "check" in r)
+    dec_ok = all(r["check"]["passed"] for dd in (dec_ep, fine_dec_ep) if dd for r in dd["runs"] if "check" in r)
     paths_ok = all(r["check"]["passed"] for r in res.values())
     return 0 if paths_ok and fine_ok and dec_ok else 1
 
@@ -700,7 +706,7 @@ def ep_phases(torch, blk, x, n=5):
 
 
 def ep_decode_measure(rb, torch, dist, device, rank, world, batches=(1, 32), prompt_len=512, new_tokens=64,
-                      seed=3):
+                      seed=3, cfg=None, name="mixtral-8x7b"):
     """Mixtral-8x7B decoding (32 layers, synthetic weights seed 3 as in
     decode_measure) expert parallel over the ranks: each rank keeps 8 / world
     experts of every layer plus replicated attention, norms, embedding and LM
@@ -713,7 +719,7 @@ def ep_decode_measure(rb, torch, dist, device, rank, world, batches=(1, 32), pro
     expert-parallel prefill logits against it."""
     from riallm_b200 import decoder as D
     from riallm_b200.ep import ExpertParallelMoE, expert_range
-    cfg = D.DecoderConfig.mixtral_8x7b()
+    cfg = cfg or D.DecoderConfig.mixtral_8x7b()
     dev = device.index or 0
     t0 = time.perf_counter()
     qw = D.synthetic_model(cfg, seed=seed, device=str(device))
@@ -743,7 +749,7 @@ def ep_decode_measure(rb, torch, dist, device, rank, world, batches=(1, 32), pro
     ep = ExpertParallelMoE(None, cfg.experts, cfg.top_k)
     model = D.Decoder(cfg, local, max_batch=max(batches), max_seq=prompt_len + new_tokens + 3, device=dev, ep=ep)
     del local
-    out = {"model": f"mixtral-8x7b: 32 layers, synthetic weights (seed {seed}), experts NF4 ({e_l} per GPU), "
+    out = {"model": f"{name}: {cfg.layers} layers, synthetic weights (seed {seed}), experts NF4 ({e_l} per GPU), "
                     "attention/embedding bf16 replicated", "prompt_tokens": prompt_len, "new_tokens": new_tokens,
            "build_s": round(build_s, 2), "runs": []}
 
@@ -980,14 +986,26 @@ def decode_batches(args):
     return tuple(int(v) for v in args.decode_batches.split(",") if v)
 
 
-def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_tokens=128, seed=3):
-    """Mixtral-8x7B (32 layers, 32/8 heads, V=32000) NF4 decoding, weights
-    resident in HBM: prefill a prompt of `prompt_len` ids, then `new_tokens`
-    decode steps replayed from one CUDA graph per batch size (all layers, LM
-    head and argmax on the device), fed a seeded random continuation. Timed
-    with CUDA events on the decoding stream."""
+def fine_model_config():
+    """The fine-grained model's shapes: 48 layers, hidden 2048, 32/4 heads
+    (head_dim 64), 128 experts, top-8, intermediate 768, V 32000."""
     from riallm_b200 import decoder as D
-    cfg = D.DecoderConfig.mixtral_8x7b()
+    return D.DecoderConfig(layers=48, hidden=2048, heads=32, kv_heads=4, head_dim=64, eps=1e-5, theta=1e6,
+                           vocab=32000, experts=128, top_k=8, intermediate=768)
+
+
+FINE_BYTES_PER_EXPERT = int(3 * 2048 * 768 * NF4_BYTES_PER_WEIGHT)  # 2,949,120
+
+
+def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_tokens=128, seed=3, cfg=None,
+                   bytes_per_expert=BYTES_PER_EXPERT, name="mixtral-8x7b"):
+    """Mixtral-8x7B (32 layers, 32/8 heads, V=32000; or `cfg`) NF4 decoding,
+    weights resident in HBM: prefill a prompt of `prompt_len` ids, then
+    `new_tokens` decode steps replayed from one CUDA graph per batch size
+    (all layers, LM head and argmax on the device), fed a seeded random
+    continuation. Timed with CUDA events on the decoding stream."""
+    from riallm_b200 import decoder as D
+    cfg = cfg or D.DecoderConfig.mixtral_8x7b()
     hbm_peak = load_peaks()[0]
     t0 = time.perf_counter()
     qw = D.synthetic_model(cfg, seed=seed, device=str(device))
@@ -997,7 +1015,8 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
     del qw
     attn_bytes = ((cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim * cfg.hidden + cfg.hidden * cfg.heads * cfg.head_dim) * 2
     lm_bytes = cfg.vocab * cfg.hidden * 2
-    out = {"model": "mixtral-8x7b: 32 layers, synthetic weights (seed 3), experts NF4, attention/embedding bf16",
+    out = {"model": f"{name}: {cfg.layers} layers, synthetic weights (seed {seed}), experts NF4, "
+                    "attention/embedding bf16",
            "prompt_tokens": prompt_len, "new_tokens": new_tokens, "build_s": round(build_s, 2), "runs": []}
     g = torch.Generator().manual_seed(seed)
 
@@ -1028,7 +1047,7 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
         used = model.experts_per_layer(cont[new_tokens])
         U = sum(used) / len(used)
         kv_read = B * cfg.kv_heads * (prompt_len + new_tokens // 2) * cfg.head_dim * 2 * 2
-        step_bytes = sum(u * BYTES_PER_EXPERT for u in used) + cfg.layers * (attn_bytes + kv_read) + lm_bytes
+        step_bytes = sum(u * bytes_per_expert for u in used) + cfg.layers * (attn_bytes + kv_read) + lm_bytes
         gbs = step_bytes / (ms_tok / 1000.0) / 1e9
         pms = p0.elapsed_time(p1)
         out["runs"].append({
@@ -1038,7 +1057,7 @@ def decode_measure(rb, torch, device, batches=(1, 32), prompt_len=512, new_token
             "step_bytes": int(step_bytes), "achieved_gbs": round(gbs, 1), "frac_hbm": round(gbs / hbm_peak, 4),
             "experts_per_layer": round(U, 2),
             "bytes_note": "per decode step: the NF4 experts each layer routed to (counted on one more step) + "
-                          "32 x (bf16 attention weights + mean KV-cache read) + LM head"})
+                          f"{cfg.layers} x (bf16 attention weights + mean KV-cache read) + LM head"})
     model.close()
     del model
     torch.cuda.empty_cache()
@@ -1222,6 +1241,8 @@ def parse_args(argv=None):
                     help="with --quant-only: the first K experts' slice of gate_up_proj instead of all 8")
     ap.add_argument("--fine-grained-only", action="store_true",
                     help="only the 128-expert top-8 measurement (prints {\"fine_grained\": ...})")
+    ap.add_argument("--fine-model-only", action="store_true",
+                    help="only the 48-layer fine-grained model decode (prints {\"fine_model_decode\": ...})")
     ap.add_argument("--stream-model-only", action="store_true",
                     help="only the reduced-depth streamed Mixtral-8x22B decode (prints {\"streaming_model\": ...})")
     ap.add_argument("--decode-only", action="store_true",
@@ -1245,6 +1266,14 @@ def main():
         torch.cuda.set_device(local)
         r = decode_measure(rb, torch, torch.device("cuda", local), decode_batches(args), new_tokens=args.decode_new)
         print(json.dumps({"decode": r}), flush=True)
+        return 0
+    if args.fine_model_only:
+        import torch
+        import riallm_b200 as rb
+        torch.cuda.set_device(local)
+        r = decode_measure(rb, torch, torch.device("cuda", local), (1, 64), prompt_len=128, new_tokens=32, seed=4,
+                           cfg=fine_model_config(), bytes_per_expert=FINE_BYTES_PER_EXPERT, name="fine-grained")
+        print(json.dumps({"fine_model_decode": r}), flush=True)
         return 0
     if args.stream_model_only:
         import torch

@@ -484,11 +484,13 @@ cudaError_t launch_router(const RouterArgs& a, int gate_qtype, cudaStream_t stre
   return launch_router_tt<1, 1>(a, gate_qtype, smem, stream);
 }
 
-// One warp per pair row; 16-byte copies. With pair_perm each 16-byte
-// group of 8 bf16 values is reordered to [0,4,1,5,2,6,3,7].
-// Row blockIdx.x of x_perm, 16-byte chunks blockIdx.y * 256 + threadIdx.x.
+// One warp per pair row, 8 rows per CTA; each lane issues up to eight of
+// its row's 16-byte loads before their stores (one 16-byte copy per thread
+// and a CTA per row left the copy latency-bound at 0.57 of HBM). With
+// pair_perm each 16-byte group of 8 bf16 values is reordered to
+// [0,4,1,5,2,6,3,7].
 __global__ void __launch_bounds__(256) gather_kernel(const void* __restrict__ x, int x_bf16,
-                                                     const int* __restrict__ perm_pair, int k, int H,
+                                                     const int* __restrict__ perm_pair, int k, int P, int H,
                                                      void* __restrict__ x_perm, int pair_perm,
                                                      const int* __restrict__ row_begin,
                                                      const int* __restrict__ row_end) {
@@ -497,26 +499,35 @@ __global__ void __launch_bounds__(256) gather_kernel(const void* __restrict__ x,
   // may start now.
   pdl_wait();
   pdl_launch_dependents();
-  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= P) return;
   // Expert-parallel calls gather only the rows of this rank's experts.
   if (row_begin && (row < __ldg(row_begin) || row >= __ldg(row_end))) return;
   const int esz = x_bf16 ? 2 : 4;
   const int n16 = H * esz / 16;
-  const int i = blockIdx.y * blockDim.x + threadIdx.x;
-  if (i >= n16) return;
   const int t = __ldg(perm_pair + row) / k;
   const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(x) + (uint64_t)t * H * esz);
   uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(x_perm) + (uint64_t)row * H * esz);
-  const uint4 v = __ldg(src + i);
-  if (pair_perm) {
-    uint4 o;
-    o.x = prmt(v.x, v.z, 0x5410u);
-    o.y = prmt(v.x, v.z, 0x7632u);
-    o.z = prmt(v.y, v.w, 0x5410u);
-    o.w = prmt(v.y, v.w, 0x7632u);
-    dst[i] = o;
-  } else {
-    dst[i] = v;
+  for (int i0 = lane; i0 < n16; i0 += 32 * 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + 32 * u < n16) v[u] = __ldg(src + i0 + 32 * u);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (i0 + 32 * u >= n16) break;
+      if (pair_perm) {
+        uint4 o;
+        o.x = prmt(v[u].x, v[u].z, 0x5410u);
+        o.y = prmt(v[u].x, v[u].z, 0x7632u);
+        o.z = prmt(v[u].y, v[u].w, 0x5410u);
+        o.w = prmt(v[u].y, v[u].w, 0x7632u);
+        dst[i0 + 32 * u] = o;
+      } else {
+        dst[i0 + 32 * u] = v[u];
+      }
+    }
   }
 }
 
@@ -524,9 +535,8 @@ cudaError_t launch_gather(const void* x, bool x_bf16, const int* perm_pair, int 
                           void* x_perm, bool pair_perm, cudaStream_t stream, const int* row_begin,
                           const int* row_end) {
   if (P == 0) return cudaSuccess;
-  const int n16 = H * (x_bf16 ? 2 : 4) / 16;
-  const dim3 grid(P, (n16 + 255) / 256);
-  cudaError_t e = launch_pdl(gather_kernel, grid, dim3(256), 0, stream, x, x_bf16 ? 1 : 0, perm_pair, k, H,
+  const dim3 grid((P + 7) / 8);
+  cudaError_t e = launch_pdl(gather_kernel, grid, dim3(256), 0, stream, x, x_bf16 ? 1 : 0, perm_pair, k, P, H,
                              x_perm, (pair_perm && x_bf16) ? 1 : 0, row_begin, row_end);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
