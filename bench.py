@@ -186,8 +186,10 @@ def config_dict(args, world):
             "hidden": H, "intermediate": I, "experts": E, "top_k": TOP_K,
             "tokens_per_step_per_gpu": args.tokens, "compression": "FourBit (riallm NF4 layout)",
             "parallelism": (f"ep{world} (expert-parallel: {E // max(world, 1)} experts per GPU; "
-                            + ("tokens all-gathered, partials reduce-scattered over NCCL)" if args.ep_path == "replicated"
-                               else "token all-to-all over NCCL inside the library)")) if world > 1 else "single",
+                            + {"replicated": "tokens all-gathered, partials reduce-scattered over NCCL)",
+                               "all_to_all": "token all-to-all over NCCL inside the library)",
+                               "all_to_all_peer": "token all-to-all by the library's stores into peer memory)"}[
+                                   args.ep_path]) if world > 1 else "single",
             "l2_policy": "inputs larger than L2 (880.8 MB of NF4 weights per step vs 126 MB L2)"}
 
 
@@ -505,7 +507,10 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
       all_to_all: each rank routes its own tokens and exchanges only the
         routed rows and their expert outputs (riallm_cuda_moe_forward_ep_a2a,
         NCCL inside the library; one host synchronisation per call for the
-        message sizes).
+        message sizes);
+      all_to_all_peer: the same exchange by the library's own kernels,
+        storing the rows into the peers' IPC-mapped buffers over NVLink
+        (riallm_cuda_moe_forward_ep_peer; no host synchronisation).
 
     --ep-path picks the one the line's value, roofline and e2e report (the
     replicated one by default: faster at decode batch sizes); the other is
@@ -531,11 +536,13 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
             rep = ExpertParallelMoE(local_w, E, TOP_K)
             made[name] = (lambda v: rep(v, ctx=ctx_rep), ctx_rep, ctx_rep.close)
         else:
-            a2a = ExpertParallelA2A(local_w, E, TOP_K, device=local)
+            a2a = ExpertParallelA2A(local_w, E, TOP_K, device=local,
+                                    transport="peer" if name == "all_to_all_peer" else "nccl", max_tokens=args.tokens)
             made[name] = (a2a, a2a.ctx, a2a.close)
         return made[name]
     head = args.ep_path
-    order = [head] + ([] if args.no_sweep else [p for p in ("replicated", "all_to_all") if p != head])
+    order = [head] + ([] if args.no_sweep else
+                      [p for p in ("replicated", "all_to_all", "all_to_all_peer") if p != head])
     res, clk = {}, None
     for name in order:
         fn, ctx, _ = make(name)
@@ -549,6 +556,7 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
         else:
             ms = timed(torch, lambda: fn(x), args.steps, args.warmup, dist, world)
         ph = ep_phases(torch, _EpCall(fn, ctx), x, n=10)
+        ctx.synchronize()  # raises if a bounded device wait of the path expired
         lib_ms = sum(ph.values())
         res[name] = {"tokens_per_s": round(world * args.tokens * args.steps / (ms / 1000.0), 1),
                      "ms_per_step": round(ms / args.steps, 4), "launches_per_step": launches,
@@ -804,18 +812,21 @@ def ep_fine_measure(rb, torch, dist, device, rank, world, steps=10):
     local_w = {"mlp.gate.weight": d["mlp.gate.weight"],
                "mlp.experts.gate_up_proj": d["mlp.experts.gate_up_proj"].expert_slice(e_b, e_l),
                "mlp.experts.down_proj": d["mlp.experts.down_proj"].expert_slice(e_b, e_l)}
-    blk = ExpertParallelA2A(local_w, Ef, kf, device=device.index or 0)
     out = {"config": f"fine-grained: hidden 2048, 128 experts, top-8, intermediate 768, NF4; {e_l} experts per GPU",
            "runs": []}
-    for T in (64, 8192):
-        gx = torch.Generator(device=device).manual_seed(4000 + T + 7919 * rank)
-        x = torch.randn(T, Hf, device=device, generator=gx).to(torch.bfloat16)
-        ms = timed(torch, lambda: blk(x), steps, 3, dist, world)
-        ph = ep_phases(torch, blk, x)
-        chk = ep_compare(torch, dist, blk(x), rb.apply_moe(d, x, kf, Ef))
-        out["runs"].append({"tokens_per_gpu": T, "tokens_per_s": round(world * T * steps / (ms / 1000.0), 1),
-                            "ms_per_step": round(ms / steps, 4), "phase_ms_per_step": ph, "check": chk})
-    blk.close()
+    for transport in ("nccl", "peer"):
+        blk = ExpertParallelA2A(local_w, Ef, kf, device=device.index or 0, transport=transport, max_tokens=8192)
+        for T in (64, 8192):
+            gx = torch.Generator(device=device).manual_seed(4000 + T + 7919 * rank)
+            x = torch.randn(T, Hf, device=device, generator=gx).to(torch.bfloat16)
+            ms = timed(torch, lambda: blk(x), steps, 3, dist, world)
+            ph = ep_phases(torch, blk, x)
+            chk = ep_compare(torch, dist, blk(x), rb.apply_moe(d, x, kf, Ef))
+            blk.ctx.synchronize()  # raises if a bounded wait of the call expired
+            out["runs"].append({"transport": transport, "tokens_per_gpu": T,
+                                "tokens_per_s": round(world * T * steps / (ms / 1000.0), 1),
+                                "ms_per_step": round(ms / steps, 4), "phase_ms_per_step": ph, "check": chk})
+        blk.close()
     del d, local_w
     torch.cuda.empty_cache()
     return out
@@ -1229,7 +1240,7 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--tokens", type=int, default=64)
-    ap.add_argument("--ep-path", choices=("replicated", "all_to_all"), default="replicated",
+    ap.add_argument("--ep-path", choices=("replicated", "all_to_all", "all_to_all_peer"), default="replicated",
                     help="expert-parallel design the multi-GPU line reports (the other is timed beside it)")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--skip-cpu-baseline", action="store_true")

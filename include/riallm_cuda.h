@@ -331,6 +331,27 @@ int32_t riallm_cuda_moe_forward_ep_a2a(riallm_ctx* ctx, const riallm_moe_weights
                                        void* out, int32_t T, int32_t H, int32_t I, int32_t E, int32_t k,
                                        uint32_t flags, void* stream);
 
+/* Peer-memory transport for the same block (collective: every rank calls
+ * it after riallm_cuda_ep_init, with the same arguments). Allocates this
+ * rank's symmetric buffer for calls of up to max_tokens tokens of this
+ * shape (flags, the rows it can receive, its pairs' returned rows), maps
+ * every peer's through CUDA IPC (handles exchanged over the communicator)
+ * and the local plan and expert buffers. Calling it again replaces the
+ * set-up; riallm_cuda_ep_destroy frees it. */
+int32_t riallm_cuda_ep_peer_init(riallm_ctx* ctx, int32_t max_tokens, int32_t H, int32_t I, int32_t E, int32_t k);
+/* riallm_cuda_moe_forward_ep_a2a's block over the peer-memory transport:
+ * the pair counts are all-gathered on the device (NCCL), each pair row is
+ * stored straight into its expert's rank's receive area and each output row
+ * into its token's rank's return area by the library's kernels (plain
+ * stores to mapped peer memory over NVLink), and the ranks hand the buffers
+ * back and forth with epoch flags (bounded waits: RIALLM_ERR_TIMEOUT through
+ * riallm_cuda_stream_synchronize). No host synchronisation, so a call can
+ * be captured in a CUDA graph. T <= max_tokens (ranks may differ); the
+ * shape must be riallm_cuda_ep_peer_init's. Routed experts only. */
+int32_t riallm_cuda_moe_forward_ep_peer(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x,
+                                        void* out, int32_t T, int32_t H, int32_t I, int32_t E, int32_t k,
+                                        uint32_t flags, void* stream);
+
 /* Host-only helper of the exchange above (no device work): from the pair
  * counts each rank sends to this rank, recv_counts[s * e_local + e] (rank s,
  * local expert e), where the received rows go: expert_counts[e],

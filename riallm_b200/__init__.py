@@ -107,6 +107,9 @@ SIGNATURES = {
     "riallm_cuda_moe_forward_ep_a2a": (_i32, [_vp, ctypes.POINTER(CMoeWeights), _vp, _vp, _i32, _i32, _i32,
                                               _i32, _i32, _u32, _vp]),
     "riallm_ep_exchange_plan": (_i32, [_i32, _i32, _vp, _vp, _vp, _vp]),
+    "riallm_cuda_ep_peer_init": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32]),
+    "riallm_cuda_moe_forward_ep_peer": (_i32, [_vp, ctypes.POINTER(CMoeWeights), _vp, _vp, _i32, _i32, _i32,
+                                               _i32, _i32, _u32, _vp]),
     "riallm_cuda_event_create": (_i32, [_vp, _pp]),
     "riallm_cuda_event_destroy": (_i32, [_vp, _vp]),
     "riallm_cuda_event_record": (_i32, [_vp, _vp, _vp]),

@@ -775,6 +775,47 @@ int32_t riallm_cuda_moe_forward_ep_a2a(riallm_ctx* ctx, const riallm_moe_weights
   return RIALLM_OK;
 }
 
+int32_t riallm_cuda_moe_forward_ep_peer(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x, void* out,
+                                        int32_t T, int32_t H, int32_t I, int32_t E, int32_t k, uint32_t flags,
+                                        void* stream) {
+  if (!ctx || !w) return RIALLM_ERR_INVALID;
+  if (!ctx->ep_peer) return set_err(ctx, RIALLM_ERR_CONFIG, "riallm_cuda_ep_peer_init was not called on this context");
+  if (T < 1 || T > ctx->ep_peer_T || H != ctx->ep_peer_H || I != ctx->ep_peer_I || E != ctx->ep_peer_E ||
+      k != ctx->ep_peer_k)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "call shape differs from riallm_cuda_ep_peer_init's (or T > its max_tokens)");
+  if (!x || !out) return set_err(ctx, RIALLM_ERR_INVALID, "null x/out");
+  if (int s = check_shapes(ctx, T, H, I, E, k)) return s;
+  const int W = ctx->ep_world, EL = E / W;
+  if (w->shared_gate_proj.data != nullptr)
+    return set_err(ctx, RIALLM_ERR_CONFIG, "expert-parallel calls take routed experts only");
+  if (int s = check_qtensor(ctx, w->gate, (uint64_t)E * H, "mlp.gate.weight", false)) return s;
+  if (int s = check_qtensor(ctx, w->gate_up_proj, (uint64_t)EL * 2 * I * H, "mlp.experts.gate_up_proj", true))
+    return s;
+  if (int s = check_qtensor(ctx, w->down_proj, (uint64_t)EL * H * I, "mlp.experts.down_proj", true)) return s;
+  if (!aligned16(x) || !aligned16(out)) return set_err(ctx, RIALLM_ERR_INVALID, "x/out must be 16-byte aligned");
+  if (int s = set_device(ctx)) return s;
+  const int P = T * k;
+  MoeLayout L = rl::moe_layout(T, H, I, E, k, RIALLM_DTYPE_BF16, 0, ctx->num_sms);
+  if (int s = ensure_arena(ctx, L.total)) return s;
+  char* base = (char*)ctx->arena;
+  cudaStream_t st = (cudaStream_t)stream;
+  {
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_ROUTE);
+    if (int s = route_into(ctx, w->gate, x, T, H, E, k, true, base, L, st)) return s;
+    ctx->launches += 1;
+  }
+  {
+    rl::PhaseTimer ps(ctx, st, RIALLM_PHASE_GATHER);
+    RL_CUDA(ctx, rl::launch_gather(x, true, (const int*)(base + L.perm_pair), k, P, H, base + L.x_perm,
+                                   w->gate_up_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT, st),
+            "gather");
+    ctx->launches += 1;
+  }
+  if (int s = rl_ep_peer_forward(ctx, w, out, T, H, I, E, k, flags, st, base, L)) return s;
+  if (ctx->profiling) ctx->profiled_calls += 1;
+  return RIALLM_OK;
+}
+
 int32_t riallm_cuda_event_create(riallm_ctx* ctx, void** event_out) {
   if (!ctx || !event_out) return RIALLM_ERR_INVALID;
   if (int s = set_device(ctx)) return s;

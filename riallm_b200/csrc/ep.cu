@@ -35,6 +35,7 @@
 #include <string>
 #include <vector>
 
+#include "common.cuh"
 #include "internal.h"
 
 namespace {
@@ -48,6 +49,7 @@ struct NcclApi {
   ncclResult_t (*GroupEnd)() = nullptr;
   ncclResult_t (*Send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
   ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
   bool ok = false;
 };
@@ -68,9 +70,10 @@ NcclApi& nccl() {
     api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
     api.Send = reinterpret_cast<decltype(api.Send)>(sym("ncclSend"));
     api.Recv = reinterpret_cast<decltype(api.Recv)>(sym("ncclRecv"));
+    api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));
     api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
     api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.CommGetAsyncError && api.GroupStart &&
-             api.GroupEnd && api.Send && api.Recv && api.GetErrorString;
+             api.GroupEnd && api.Send && api.Recv && api.AllGather && api.GetErrorString;
   });
   return api;
 }
@@ -123,6 +126,9 @@ int rl_ep_plan(int world, int e_local, const int32_t* recv_counts, int32_t* expe
   return RIALLM_OK;
 }
 
+// Frees the peer transport of a context (defined with the transport below).
+static void peer_teardown_ctx(riallm_ctx* ctx);
+
 extern "C" {
 
 int32_t riallm_ep_exchange_plan(int32_t world, int32_t e_local, const int32_t* recv_counts,
@@ -162,6 +168,7 @@ int32_t riallm_cuda_ep_destroy(riallm_ctx* ctx) {
   if (!ctx) return RIALLM_ERR_INVALID;
   if (!ctx->ep_comm) return RIALLM_OK;
   cudaSetDevice(ctx->device);
+  peer_teardown_ctx(ctx);
   nccl().CommDestroy(static_cast<ncclComm_t>(ctx->ep_comm));
   ctx->ep_comm = nullptr;
   if (ctx->ep_arena) cudaFree(ctx->ep_arena);
@@ -416,3 +423,472 @@ uint64_t rl_ep_extra_bytes(int T, int H, int I, int E, int k, int W, int num_sms
   (void)T, (void)H, (void)I, (void)k, (void)num_sms;
   return align_up((uint64_t)W * (E / W) * 4, 1024) + 1024;
 }
+
+// ===================================================== peer-memory transport
+//
+// The same exchange without NCCL on the data path and without a host
+// synchronisation, so a call can be captured in a CUDA graph. Every rank
+// owns a symmetric buffer (the same layout on every rank) that its peers map
+// through CUDA IPC: four arrays of W epoch flags and the receive areas for
+// token rows (expert-major) and for returned output rows (this rank's
+// expert-sorted pair order). A call:
+//
+//   1. all-gathers the W x E pair-count matrix (NCCL, on the stream);
+//   2. plan kernel: bumps the call's epoch n, derives from the matrix where
+//      each of this rank's rows lands at its owner and where each received
+//      row goes back, then waits until every receiver has consumed this
+//      rank's rows of call n-1 (free_x);
+//   3. dispatch kernel: copies each pair row straight into its owner's
+//      receive area with stores over NVLink; the CTA that finishes last
+//      publishes arrived_x = n at every peer (release, system scope);
+//   4. waits for arrived_x = n from every peer, runs the expert GEMMs,
+//      tells every sender its rows were consumed (free_x = n);
+//   5. waits until every home rank has consumed call n-1's returns (free_y),
+//      copies each output row into its home rank's return area at the
+//      pair's own position, publishes arrived_y = n;
+//   6. waits for arrived_y = n from every peer, combines, publishes
+//      free_y = n.
+//
+// Every wait is bounded (RIALLM_ERR_TIMEOUT in the context's status word);
+// every peer address is bounds-checked against the receive areas before it
+// is stored to. Stores are plain st.global to mapped peer memory: no TMA,
+// no multicast.
+namespace {
+
+constexpr int kArrX = 0, kArrY = 1, kFreeX = 2, kFreeY = 3;
+constexpr uint64_t kPeerWaitNs = 5000ull * 1000ull * 1000ull;  // 5 s
+
+struct PeerLayout {
+  int cap_x, cap_y, maxp;
+  // symmetric buffer
+  uint64_t flags, xr, ret, total;
+  // local buffer
+  uint64_t epoch, done, cmat, dest_base, ecnt, eoff, rcv_pos, ret_base, peers, hr, yr, skw, ltotal;
+};
+
+PeerLayout peer_layout(int W, int T, int H, int I, int E, int k, int num_sms) {
+  PeerLayout p{};
+  const int EL = E / W;
+  p.cap_x = W * T * (k < EL ? k : EL);  // rows this rank can receive
+  p.cap_y = T * k;                      // this rank's own pairs
+  p.maxp = W * T < p.cap_x ? W * T : p.cap_x;  // an expert gets at most one pair per token
+  uint64_t o = 0;
+  auto take = [&](uint64_t b) {
+    const uint64_t r = o;
+    o = align_up(o + b, 1024);
+    return r;
+  };
+  p.flags = take(4ull * W * 8);
+  p.xr = take((uint64_t)p.cap_x * H * 2);
+  p.ret = take((uint64_t)p.cap_y * H * 4);
+  p.total = o;
+  o = 0;
+  p.epoch = take(8);
+  p.done = take(16);
+  p.cmat = take((uint64_t)W * E * 4);
+  p.dest_base = take((uint64_t)E * 4);
+  p.ecnt = take((uint64_t)EL * 4);
+  p.eoff = take((uint64_t)(EL + 1) * 4);
+  p.rcv_pos = take((uint64_t)W * EL * 4);
+  p.ret_base = take((uint64_t)W * EL * 4);
+  p.peers = take((uint64_t)W * 8);
+  p.hr = take((uint64_t)p.cap_x * I * 2);
+  p.yr = take((uint64_t)p.cap_x * H * 4);
+  p.skw = take(rl::tc_sk_ws_bytes(num_sms, p.maxp));
+  p.ltotal = o;
+  return p;
+}
+
+__device__ __forceinline__ uint64_t* flag_at(char* sym_base, int which, int W, int from) {
+  return reinterpret_cast<uint64_t*>(sym_base) + which * W + from;
+}
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Thread 0: waits, at most limit_ns, until flags[0..W) >= target; records
+// RIALLM_ERR_TIMEOUT otherwise.
+__device__ void wait_peer_flags(const uint64_t* flags, int W, uint64_t target, uint64_t limit_ns, int* status) {
+  const uint64_t t0 = rl::globaltimer_ns();
+  for (;;) {
+    bool ok = true;
+    for (int s = 0; s < W && ok; ++s) ok = ld_acquire_sys(flags + s) >= target;
+    if (ok) return;
+    if (rl::globaltimer_ns() - t0 > limit_ns) {
+      atomicExch(status, RIALLM_ERR_TIMEOUT);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
+struct PeerArgs {
+  char* const* peers;  // [W] symmetric bases, this rank's own at [me]
+  char* sym;           // this rank's symmetric base
+  char* loc;           // this rank's local buffer
+  int* status;
+  uint64_t wait_ns;
+  int W, me, E, EL;
+  PeerLayout L;
+};
+
+// Step 2 (one thread): epoch, plan, then wait for free_x >= n - 1.
+__global__ void ep_peer_plan_kernel(PeerArgs a) {
+  if (threadIdx.x != 0) return;
+  uint64_t* epoch = reinterpret_cast<uint64_t*>(a.loc + a.L.epoch);
+  const uint64_t n = *epoch + 1;
+  *epoch = n;
+  const int W = a.W, E = a.E, EL = a.EL, me = a.me;
+  const int* C = reinterpret_cast<const int*>(a.loc + a.L.cmat);  // C[s * E + e]: rank s's pairs of expert e
+  int* dest_base = reinterpret_cast<int*>(a.loc + a.L.dest_base);
+  int* ecnt = reinterpret_cast<int*>(a.loc + a.L.ecnt);
+  int* eoff = reinterpret_cast<int*>(a.loc + a.L.eoff);
+  int* rcv_pos = reinterpret_cast<int*>(a.loc + a.L.rcv_pos);
+  int* ret_base = reinterpret_cast<int*>(a.loc + a.L.ret_base);
+  // This rank's receive area: its experts in order, ranks ascending inside
+  // an expert.
+  int off = 0;
+  for (int el = 0; el < EL; ++el) {
+    const int e = me * EL + el;
+    eoff[el] = off;
+    int c = 0;
+    for (int s = 0; s < W; ++s) {
+      rcv_pos[s * EL + el] = off + c;
+      c += C[s * E + e];
+    }
+    ecnt[el] = c;
+    off += c;
+  }
+  eoff[EL] = off;
+  // Where this rank's rows of expert e start in the owner's receive area.
+  for (int r = 0; r < W; ++r) {
+    int o = 0;
+    for (int el = 0; el < EL; ++el) {
+      const int e = r * EL + el;
+      int before = 0;
+      for (int s = 0; s < me; ++s) before += C[s * E + e];
+      dest_base[e] = o + before;
+      for (int s = 0; s < W; ++s) o += C[s * E + e];
+    }
+  }
+  // Where rank s's pairs of this rank's expert e sit in s's expert-sorted
+  // order (s's router offsets: the prefix of its counts).
+  for (int s = 0; s < W; ++s) {
+    int o = 0;
+    for (int e = 0; e < E; ++e) {
+      if (e / EL == me) ret_base[s * EL + (e - me * EL)] = o;
+      o += C[s * E + e];
+    }
+  }
+  wait_peer_flags(flag_at(a.sym, kFreeX, W, 0), W, n - 1, a.wait_ns, a.status);
+}
+
+// Thread 0: wait until flags[which][0..W) of this rank >= epoch - back.
+__global__ void ep_peer_wait_kernel(PeerArgs a, int which, int back) {
+  if (threadIdx.x != 0) return;
+  const uint64_t n = *reinterpret_cast<const uint64_t*>(a.loc + a.L.epoch);
+  wait_peer_flags(flag_at(a.sym, which, a.W, 0), a.W, n - back, a.wait_ns, a.status);
+}
+
+// Lane s < W: flags[which][me] of rank s = epoch.
+__global__ void ep_peer_signal_kernel(PeerArgs a, int which) {
+  const int s = threadIdx.x;
+  if (s >= a.W) return;
+  const uint64_t n = *reinterpret_cast<const uint64_t*>(a.loc + a.L.epoch);
+  __threadfence_system();
+  st_release_sys(flag_at(a.peers[s], which, a.W, a.me), n);
+}
+
+// The last CTA to finish (a local counter it resets) publishes `which` = n at
+// every peer, after every CTA's stores were fenced at system scope.
+__device__ void publish_when_done(const PeerArgs& a, int counter, int which) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned* done = reinterpret_cast<unsigned*>(a.loc + a.L.done) + counter;
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      __threadfence_system();
+      const uint64_t n = *reinterpret_cast<const uint64_t*>(a.loc + a.L.epoch);
+      for (int s = 0; s < a.W; ++s) st_release_sys(flag_at(a.peers[s], which, a.W, a.me), n);
+      *done = 0;
+    }
+  }
+}
+
+// Copies `row_bytes` (a multiple of 16) from src to dst, one warp.
+__device__ __forceinline__ void warp_copy_row(const char* __restrict__ src, char* dst, uint64_t row_bytes,
+                                              int lane) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  const int n16 = (int)(row_bytes / 16);
+  for (int i0 = lane; i0 < n16; i0 += 32 * 8) {
+    uint4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + 32 * u < n16) v[u] = __ldcs(s + i0 + 32 * u);
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (i0 + 32 * u < n16) d[i0 + 32 * u] = v[u];
+  }
+}
+
+// Step 3: pair row i of x_perm (expert e = the one whose offsets range holds
+// i) to its owner's receive area.
+__global__ void __launch_bounds__(256) ep_peer_dispatch_kernel(PeerArgs a, const char* __restrict__ x_perm,
+                                                               const int* __restrict__ offsets, int P,
+                                                               uint64_t rowb) {
+  const int lane = threadIdx.x & 31;
+  const int* dest_base = reinterpret_cast<const int*>(a.loc + a.L.dest_base);
+  for (int i = blockIdx.x * 8 + (threadIdx.x >> 5); i < P; i += gridDim.x * 8) {
+    int lo = 0, hi = a.E;  // largest e with offsets[e] <= i
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (__ldg(offsets + mid) <= i) lo = mid;
+      else hi = mid;
+    }
+    const int e = lo, r = e / a.EL;
+    const int row = dest_base[e] + (i - __ldg(offsets + e));
+    if (row < 0 || row >= a.L.cap_x || r >= a.W) {
+      if (lane == 0) atomicExch(a.status, RIALLM_ERR_INVALID);
+      continue;
+    }
+    warp_copy_row(x_perm + (uint64_t)i * rowb, a.peers[r] + a.L.xr + (uint64_t)row * rowb, rowb, lane);
+  }
+  publish_when_done(a, 0, kArrX);
+}
+
+// Step 5: received row q (expert el, from rank s, its j-th pair of that
+// expert) back to position ret_base[s][el] + j of rank s's return area.
+__global__ void __launch_bounds__(256) ep_peer_return_kernel(PeerArgs a, uint64_t rowy) {
+  const int lane = threadIdx.x & 31;
+  const int* C = reinterpret_cast<const int*>(a.loc + a.L.cmat);
+  const int* eoff = reinterpret_cast<const int*>(a.loc + a.L.eoff);
+  const int* rcv_pos = reinterpret_cast<const int*>(a.loc + a.L.rcv_pos);
+  const int* ret_base = reinterpret_cast<const int*>(a.loc + a.L.ret_base);
+  const char* yr = a.loc + a.L.yr;
+  const int R = eoff[a.EL];
+  for (int q = blockIdx.x * 8 + (threadIdx.x >> 5); q < R; q += gridDim.x * 8) {
+    int el = 0, hi = a.EL;  // largest el with eoff[el] <= q
+    while (hi - el > 1) {
+      const int mid = (el + hi) >> 1;
+      if (eoff[mid] <= q) el = mid;
+      else hi = mid;
+    }
+    const int e = a.me * a.EL + el;
+    int s = 0;
+    while (s + 1 < a.W && q >= rcv_pos[s * a.EL + el] + C[s * a.E + e]) ++s;
+    const int pos = ret_base[s * a.EL + el] + (q - rcv_pos[s * a.EL + el]);
+    if (pos < 0 || pos >= a.L.cap_y || q >= a.L.cap_x) {
+      if (lane == 0) atomicExch(a.status, RIALLM_ERR_INVALID);
+      continue;
+    }
+    warp_copy_row(yr + (uint64_t)q * rowy, a.peers[s] + a.L.ret + (uint64_t)pos * rowy, rowy, lane);
+  }
+  publish_when_done(a, 1, kArrY);
+}
+
+}  // namespace
+
+namespace {
+
+void peer_teardown(riallm_ctx* ctx) {
+  if (!ctx->ep_peer && !ctx->ep_sym && !ctx->ep_peer_local) return;
+  cudaSetDevice(ctx->device);
+  cudaDeviceSynchronize();
+  for (void* p : ctx->ep_peer_open)
+    if (p) cudaIpcCloseMemHandle(p);
+  ctx->ep_peer_open.clear();
+  if (ctx->ep_sym) cudaFree(ctx->ep_sym);
+  if (ctx->ep_peer_local) cudaFree(ctx->ep_peer_local);
+  ctx->ep_sym = nullptr;
+  ctx->ep_peer_local = nullptr;
+  ctx->ep_peer = false;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t riallm_cuda_ep_peer_init(riallm_ctx* ctx, int32_t max_tokens, int32_t H, int32_t I, int32_t E, int32_t k) {
+  if (!ctx) return RIALLM_ERR_INVALID;
+  if (!ctx->ep_comm) return fail(ctx, RIALLM_ERR_CONFIG, "riallm_cuda_ep_init was not called on this context");
+  const int W = ctx->ep_world, me = ctx->ep_rank;
+  if (max_tokens < 1 || H <= 0 || I <= 0 || E <= 0 || k <= 0 || k > E || E > 256 || k > 16 || E % W || H % 256 ||
+      I % 256)
+    return fail(ctx, RIALLM_ERR_CONFIG, "peer transport: need T >= 1, H and I multiples of 256, k <= E <= 256, "
+                                        "k <= 16 and E a multiple of the world size");
+  NcclApi& n = nccl();
+  EP_CUDA(ctx, cudaSetDevice(ctx->device), "cudaSetDevice");
+  peer_teardown(ctx);
+  const PeerLayout L = peer_layout(W, max_tokens, H, I, E, k, ctx->num_sms);
+  auto bail = [&](int code, const std::string& msg) {
+    peer_teardown(ctx);
+    return fail(ctx, code, msg);
+  };
+  if (cudaMalloc(&ctx->ep_sym, L.total) != cudaSuccess || cudaMalloc(&ctx->ep_peer_local, L.ltotal) != cudaSuccess)
+    return bail(RIALLM_ERR_CUDA, "cudaMalloc(peer transport buffers)");
+  if (cudaMemset(ctx->ep_sym, 0, L.xr) != cudaSuccess ||
+      cudaMemset(ctx->ep_peer_local, 0, L.cmat) != cudaSuccess)
+    return bail(RIALLM_ERR_CUDA, "cudaMemset(peer transport flags)");
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, ctx->ep_sym) != cudaSuccess) return bail(RIALLM_ERR_CUDA, "cudaIpcGetMemHandle");
+  // Every rank's flags are zero before any rank can learn its handle.
+  if (cudaDeviceSynchronize() != cudaSuccess) return bail(RIALLM_ERR_CUDA, "cudaDeviceSynchronize");
+  char* dh = nullptr;
+  cudaStream_t st = nullptr;
+  std::vector<cudaIpcMemHandle_t> hs(W);
+  if (cudaMalloc(&dh, (size_t)W * sizeof(h)) != cudaSuccess || cudaStreamCreate(&st) != cudaSuccess ||
+      cudaMemcpy(dh + (size_t)me * sizeof(h), &h, sizeof(h), cudaMemcpyHostToDevice) != cudaSuccess) {
+    if (dh) cudaFree(dh);
+    if (st) cudaStreamDestroy(st);
+    return bail(RIALLM_ERR_CUDA, "peer handle exchange buffers");
+  }
+  const ncclResult_t r = n.AllGather(dh + (size_t)me * sizeof(h), dh, sizeof(h), ncclUint8,
+                                     static_cast<ncclComm_t>(ctx->ep_comm), st);
+  const bool ok = r == ncclSuccess && cudaStreamSynchronize(st) == cudaSuccess &&
+                  cudaMemcpy(hs.data(), dh, (size_t)W * sizeof(h), cudaMemcpyDeviceToHost) == cudaSuccess;
+  cudaFree(dh);
+  cudaStreamDestroy(st);
+  if (!ok) return bail(RIALLM_ERR_CUDA, "peer handle exchange (ncclAllGather)");
+  std::vector<char*> bases(W, nullptr);
+  ctx->ep_peer_open.assign(W, nullptr);
+  for (int s = 0; s < W; ++s) {
+    if (s == me) {
+      bases[s] = static_cast<char*>(ctx->ep_sym);
+      continue;
+    }
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, hs[s], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess)
+      return bail(RIALLM_ERR_CUDA, "cudaIpcOpenMemHandle (peer " + std::to_string(s) + ")");
+    ctx->ep_peer_open[s] = p;
+    bases[s] = static_cast<char*>(p);
+  }
+  if (cudaMemcpy(static_cast<char*>(ctx->ep_peer_local) + L.peers, bases.data(), (size_t)W * sizeof(char*),
+                 cudaMemcpyHostToDevice) != cudaSuccess)
+    return bail(RIALLM_ERR_CUDA, "peer base upload");
+  ctx->ep_peer = true;
+  ctx->ep_peer_T = max_tokens;
+  ctx->ep_peer_H = H;
+  ctx->ep_peer_I = I;
+  ctx->ep_peer_E = E;
+  ctx->ep_peer_k = k;
+  return RIALLM_OK;
+}
+
+}  // extern "C"
+
+int rl_ep_peer_forward(riallm_ctx* ctx, const riallm_moe_weights* w, void* out, int T, int H, int I, int E, int k,
+                       uint32_t flags, cudaStream_t st, char* base, const rl::MoeLayout& L) {
+  NcclApi& n = nccl();
+  const int W = ctx->ep_world, EL = E / W, P = T * k;
+  const PeerLayout pl = peer_layout(W, ctx->ep_peer_T, H, I, E, k, ctx->num_sms);
+  char* sym = static_cast<char*>(ctx->ep_sym);
+  char* loc = static_cast<char*>(ctx->ep_peer_local);
+  PeerArgs a{};
+  a.peers = reinterpret_cast<char* const*>(loc + pl.peers);
+  a.sym = sym;
+  a.loc = loc;
+  a.status = ctx->d_status;
+  a.wait_ns = ctx->flag_wait_ns ? ctx->flag_wait_ns : kPeerWaitNs;
+  a.W = W;
+  a.me = ctx->ep_rank;
+  a.E = E;
+  a.EL = EL;
+  a.L = pl;
+  const uint64_t rowb = (uint64_t)H * 2, rowy = (uint64_t)H * 4;
+  const int* offsets = reinterpret_cast<const int*>(base + L.offsets);
+  const int cap_grid = 4 * ctx->num_sms;
+  {
+    rl::PhaseTimer pt(ctx, st, RIALLM_PHASE_DISPATCH);
+    EP_NCCL(ctx, n.AllGather(base + L.counts, loc + pl.cmat, E, ncclInt32, static_cast<ncclComm_t>(ctx->ep_comm), st),
+            "ncclAllGather(counts)");
+    ep_peer_plan_kernel<<<1, 32, 0, st>>>(a);
+    const int gd = std::max(1, std::min((P + 7) / 8, cap_grid));
+    ep_peer_dispatch_kernel<<<gd, 256, 0, st>>>(a, base + L.x_perm, offsets, P, rowb);
+    ep_peer_wait_kernel<<<1, 32, 0, st>>>(a, kArrX, 0);
+    EP_CUDA(ctx, cudaGetLastError(), "peer dispatch");
+    ctx->launches += 3;
+  }
+  rl::TcGemmArgs g{};
+  g.w = w->gate_up_proj;
+  g.K = H;
+  g.rows_per_expert = 2 * I;
+  g.a1_offset = I;
+  g.m_step = 128;
+  g.m_tiles = I / 128;
+  g.b = sym + pl.xr;
+  g.P = pl.cap_x;
+  g.counts = reinterpret_cast<const int*>(loc + pl.ecnt);
+  g.offsets = reinterpret_cast<const int*>(loc + pl.eoff);
+  g.E = EL;
+  g.swiglu = true;
+  g.h_pair_perm = w->down_proj.qtype == RIALLM_COMPRESSION_FOUR_BIT;
+  g.h_out = reinterpret_cast<uint16_t*>(loc + pl.hr);
+  g.ld_out = I;
+  g.status = ctx->d_status;
+  g.max_pairs_per_expert = pl.maxp;
+  g.sk_ws = reinterpret_cast<float*>(loc + pl.skw);
+  g.sk_flags = reinterpret_cast<int*>(base + L.sync + rl::kSkFlagsOffset);
+  g.pdl = false;
+  g.flag_wait_ns = ctx->flag_wait_ns;
+  rl::TcGemmArgs d = g;
+  d.w = w->down_proj;
+  d.K = I;
+  d.rows_per_expert = H;
+  d.a1_offset = 128;
+  d.m_step = 256;
+  d.m_tiles = H / 256;
+  d.b = loc + pl.hr;
+  d.swiglu = false;
+  d.h_pair_perm = false;
+  d.h_out = nullptr;
+  d.y_out = reinterpret_cast<float*>(loc + pl.yr);
+  d.ld_out = H;
+  d.pdl = false;  // follows the free_x signal, not the gate_up launch
+  {
+    rl::PhaseTimer pt(ctx, st, RIALLM_PHASE_GATE_UP);
+    EP_CUDA(ctx, rl::launch_tc_gemm(g, ctx->num_sms, st), "expert gate_up (tcgen05)");
+    ctx->launches += 1;
+  }
+  // The rows received this call are consumed: the senders may overwrite
+  // them in the next call.
+  ep_peer_signal_kernel<<<1, 32, 0, st>>>(a, kFreeX);
+  EP_CUDA(ctx, cudaGetLastError(), "peer free signal");
+  ctx->launches += 1;
+  {
+    rl::PhaseTimer pt(ctx, st, RIALLM_PHASE_DOWN);
+    EP_CUDA(ctx, rl::launch_tc_gemm(d, ctx->num_sms, st), "expert down (tcgen05)");
+    ctx->launches += 1;
+  }
+  {
+    rl::PhaseTimer pt(ctx, st, RIALLM_PHASE_RETURN);
+    ep_peer_wait_kernel<<<1, 32, 0, st>>>(a, kFreeY, 1);
+    const int gr = std::max(1, std::min((pl.cap_x + 7) / 8, cap_grid));
+    ep_peer_return_kernel<<<gr, 256, 0, st>>>(a, rowy);
+    ep_peer_wait_kernel<<<1, 32, 0, st>>>(a, kArrY, 0);
+    EP_CUDA(ctx, cudaGetLastError(), "peer return");
+    ctx->launches += 3;
+  }
+  {
+    rl::PhaseTimer pt(ctx, st, RIALLM_PHASE_COMBINE);
+    EP_CUDA(ctx, rl::launch_combine(reinterpret_cast<const float*>(sym + pl.ret),
+                                    reinterpret_cast<const int*>(base + L.inv_pos),
+                                    reinterpret_cast<const int*>(base + L.topk_idx),
+                                    reinterpret_cast<const float*>(base + L.topk_w), T, k, H, nullptr, nullptr, out,
+                                    true, (flags & RIALLM_MOE_ADD_TO_OUT) != 0, st, 0, 1 << 30, true),
+            "combine");
+    ctx->launches += 1;
+  }
+  // This call's returns are consumed: the expert ranks may overwrite them.
+  ep_peer_signal_kernel<<<1, 32, 0, st>>>(a, kFreeY);
+  EP_CUDA(ctx, cudaGetLastError(), "peer free signal");
+  ctx->launches += 1;
+  return RIALLM_OK;
+}
+
+static void peer_teardown_ctx(riallm_ctx* ctx) { peer_teardown(ctx); }

@@ -53,6 +53,15 @@ struct riallm_ctx {
   std::vector<int32_t> ep_host, ep_upload;
   void* ep_arena = nullptr;
   uint64_t ep_arena_bytes = 0;
+  // Peer-memory transport (riallm_cuda_ep_peer_init): the shape it was set
+  // up for, this rank's symmetric buffer (same layout on every rank, mapped
+  // by the peers through CUDA IPC), the peers' mapped bases, and this
+  // rank's local buffers (plan, epoch, counters, expert intermediates).
+  bool ep_peer = false;
+  int ep_peer_T = 0, ep_peer_H = 0, ep_peer_I = 0, ep_peer_E = 0, ep_peer_k = 0;
+  void* ep_sym = nullptr;
+  std::vector<void*> ep_peer_open;
+  void* ep_peer_local = nullptr;
 };
 
 namespace rl {
@@ -267,3 +276,8 @@ int rl_ep_forward(riallm_ctx* ctx, const riallm_moe_weights* w, const void* x, v
                   uint64_t ep_off);
 int rl_ep_plan(int world, int e_local, const int32_t* recv_counts, int32_t* expert_counts,
                int32_t* expert_offsets, int32_t* block_pos);
+// The same block over the peer-memory transport (riallm_cuda_ep_peer_init):
+// no host synchronisation; combine reads the returned rows from the
+// symmetric buffer.
+int rl_ep_peer_forward(riallm_ctx* ctx, const riallm_moe_weights* w, void* out, int T, int H, int I, int E, int k,
+                       uint32_t flags, cudaStream_t st, char* base, const rl::MoeLayout& L);

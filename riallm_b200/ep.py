@@ -28,6 +28,7 @@ import torch
 import torch.distributed as dist
 
 from . import ConfigError, RiallmError, TensorLike, apply_moe_ep_partial
+from . import _weights as _weights_of
 
 
 class RankFailureError(RiallmError):
@@ -182,9 +183,19 @@ class ExpertParallelA2A:
 
     def __init__(self, tensors: Mapping[str, TensorLike], num_experts: int, top_k: int,
                  group: Optional[dist.ProcessGroup] = None, device: Optional[int] = None,
-                 watch: Optional[PeerWatch] = None):
+                 watch: Optional[PeerWatch] = None, transport: str = "nccl", max_tokens: int = 0):
+        """transport "nccl": NCCL point-to-point moves the rows (one host
+        synchronisation per call for the message sizes). "peer": the
+        library's kernels store the rows into the peers' IPC-mapped buffers
+        (riallm_cuda_ep_peer_init, for calls of up to max_tokens tokens; no
+        host synchronisation, graph-capturable)."""
         import ctypes
         from . import Context, lib
+        if transport not in ("nccl", "peer"):
+            raise ConfigError(f"unknown transport {transport!r}")
+        if transport == "peer" and max_tokens < 1:
+            raise ConfigError("the peer transport needs max_tokens >= 1")
+        self.transport = transport
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -201,6 +212,11 @@ class ExpertParallelA2A:
         dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
         uid = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
         self.ctx.check(lib().riallm_cuda_ep_init(self.ctx.ptr, uid, self.rank, self.world))
+        if transport == "peer":
+            _, _, gu = _weights_of(tensors)
+            H, I = int(gu.shape[2]), int(gu.shape[1]) // 2
+            self.ctx.reserve(int(max_tokens), H, I, self.E, self.k, torch.bfloat16)
+            self.ctx.check(lib().riallm_cuda_ep_peer_init(self.ctx.ptr, int(max_tokens), H, I, self.E, self.k))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         import ctypes
@@ -214,9 +230,10 @@ class ExpertParallelA2A:
         w, keep, gu = _weights(self.tensors)
         I = int(gu.shape[1]) // 2
         out = torch.empty_like(x)
-        self.ctx.check(lib().riallm_cuda_moe_forward_ep_a2a(self.ctx.ptr, ctypes.byref(w), x.data_ptr(),
-                                                            out.data_ptr(), T, H, I, self.E, self.k, 0,
-                                                            _stream_ptr(x)))
+        fwd = (lib().riallm_cuda_moe_forward_ep_peer if self.transport == "peer"
+               else lib().riallm_cuda_moe_forward_ep_a2a)
+        self.ctx.check(fwd(self.ctx.ptr, ctypes.byref(w), x.data_ptr(), out.data_ptr(), T, H, I, self.E, self.k, 0,
+                           _stream_ptr(x)))
         rc = lib().riallm_cuda_ep_async_error(self.ctx.ptr)
         if rc != 0:
             raise RankFailureError(lib().riallm_cuda_last_error(self.ctx.ptr).decode())

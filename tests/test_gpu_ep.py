@@ -99,6 +99,14 @@ def _nccl_worker(rank, world, port, result_dir):
                 outs.append(a2a(x_all[rank * T:(rank + 1) * T]))
             torch.cuda.synchronize()
             a2a.close()
+            # The peer-memory transport: rows stored into the other GPU's
+            # mapped buffers by the library's kernels, three calls in a row.
+            peer = ExpertParallelA2A(_local(d, e_b, e_l), E, k, device=rank, transport="peer", max_tokens=T)
+            for _ in range(3):
+                outs.append(peer(x_all[rank * T:(rank + 1) * T]))
+            torch.cuda.synchronize()
+            peer.ctx.synchronize()
+            peer.close()
             for o in outs:
                 b_, r_ = _bf16_bound(o.float(), mine)
                 bad += b_
