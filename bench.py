@@ -784,7 +784,15 @@ def ep_decode_measure(rb, torch, dist, device, rank, world, batches=(1, 32), pro
         if rank == 0 and B == batches[0]:
             lg = logits.float().cpu().numpy()
             e = float(abs(lg - ref_logits).max() / abs(ref_logits).max())
-            run["check"] = {"prefill_logits_rel_err_vs_one_gpu": e, "tol": 2e-2, "passed": e < 2e-2}
+            agree = float((lg.argmax(-1) == ref_logits.argmax(-1)).mean())
+            # Both runs sum the same float32 terms in another order and round
+            # activations to bf16 at every layer, so an early one-ulp flip
+            # can grow over the layers: logits within 2e-2 for 32 layers,
+            # 5e-2 for deeper models, and the greedy token of at least 95 % of
+            # the sequences unchanged.
+            tol = 2e-2 if cfg.layers <= 32 else 5e-2
+            run["check"] = {"prefill_logits_rel_err_vs_one_gpu": e, "tol": tol, "greedy_agreement": agree,
+                            "passed": e < tol and agree >= 0.95}
         out["runs"].append(run)
     model.close()
     del model
