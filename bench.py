@@ -745,13 +745,13 @@ def ep_decode_measure(rb, torch, dist, device, rank, world, batches=(1, 32), pro
     dist.barrier()
     e_b, e_l = expert_range(cfg.experts, rank, world)
     local = {}
-    for name, v in qw.items():
-        if ".mlp.experts." in name:
+    for key, v in qw.items():
+        if ".mlp.experts." in key:
             sl = v.expert_slice(e_b, e_l)
-            local[name] = rb.QuantizedTensor(sl.data.clone(), tuple(sl.shape), sl.qtype, sl.scales.clone(),
-                                             sl.zero_points.clone(), sl.block_size)
+            local[key] = rb.QuantizedTensor(sl.data.clone(), tuple(sl.shape), sl.qtype, sl.scales.clone(),
+                                            sl.zero_points.clone(), sl.block_size)
         else:
-            local[name] = v
+            local[key] = v
     del qw
     torch.cuda.empty_cache()
     ep = ExpertParallelMoE(None, cfg.experts, cfg.top_k)
