@@ -543,26 +543,63 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     head = args.ep_path
     order = [head] + ([] if args.no_sweep else
                       [p for p in ("replicated", "all_to_all", "all_to_all_peer") if p != head])
-    res, clk = {}, None
+    # The replicated and peer-memory steps have no host synchronisation:
+    # they are timed as CUDA-graph replays (collectives and hand-offs
+    # included), like the one-GPU block. The NCCL all-to-all needs the
+    # message sizes on the host and runs eagerly.
+    graphs = []  # released before the handles close and the group ends
+
+    def capture(fn, xin):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn(xin)
+        torch.cuda.current_stream().wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            o = fn(xin)
+        graphs.append(g)
+        return g, o
+
+    res, clk, head_graphs = {}, None, None
+    g = gout = None
     for name in order:
         fn, ctx, _ = make(name)
         fn(x)
         l0 = ctx.launch_count()
         fn(x)
         launches = ctx.launch_count() - l0  # library kernels of one step
+        graphed = name != "all_to_all"
+        if graphed:
+            g, gout = capture(fn, x)
+            step = g.replay
+        else:
+            step = (lambda f: (lambda: f(x)))(fn)
         if name == head:
             with ClockSampler(local) as clk:
-                ms = timed(torch, lambda: fn(x), args.steps, args.warmup, dist, world)
+                ms = timed(torch, step, args.steps, args.warmup, dist, world)
         else:
-            ms = timed(torch, lambda: fn(x), args.steps, args.warmup, dist, world)
+            ms = timed(torch, step, args.steps, args.warmup, dist, world)
         ph = ep_phases(torch, _EpCall(fn, ctx), x, n=10)
         ctx.synchronize()  # raises if a bounded device wait of the path expired
         lib_ms = sum(ph.values())
+        chk = ep_verify(rb, torch, dist, d, fn, x, rank, world)
+        if graphed:
+            # The replayed step computes what the eager call does, bit for bit.
+            g.replay()
+            same = torch.tensor([1.0 if torch.equal(gout, fn(x)) else 0.0], device=device)
+            dist.all_reduce(same, op=dist.ReduceOp.MIN)
+            chk["graph_replay_equals_eager"] = bool(same.item() == 1.0)
+            chk["passed"] = chk["passed"] and chk["graph_replay_equals_eager"]
+            if name == head:
+                xs1 = x.clone()  # the e2e loop's second input buffer
+                head_graphs = [(g, gout), capture(fn, xs1)]
         res[name] = {"tokens_per_s": round(world * args.tokens * args.steps / (ms / 1000.0), 1),
                      "ms_per_step": round(ms / args.steps, 4), "launches_per_step": launches,
-                     "phase_ms_per_step": ph,
+                     "cuda_graph": graphed, "phase_ms_per_step": ph,
                      "outside_library_ms_per_step": round(max(ms / args.steps - lib_ms, 0.0), 4),
-                     "check": ep_verify(rb, torch, dist, d, fn, x, rank, world)}
+                     "check": chk}
     ms_per_step = res[head]["ms_per_step"]
     value = res[head]["tokens_per_s"]
     launches_per_step = res[head]["launches_per_step"]
@@ -593,13 +630,20 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     hx = torch.empty_like(x, device="cpu").pin_memory()
     hx.copy_(x.cpu())
     houts = [torch.empty_like(hx).pin_memory() for _ in range(2)]
-    xs = [x, torch.empty_like(x)]
+    xs = [x, xs1] if head_graphs is not None else [x, torch.empty_like(x)]
     outs = [None, None]
     comp = torch.cuda.current_stream()
     copy = torch.cuda.Stream()
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_done = [torch.cuda.Event() for _ in range(2)]
     ev_out = [torch.cuda.Event() for _ in range(2)]
+
+    def head_step(b):
+        if head_graphs is None:
+            return blk(xs[b])
+        gb, ob = head_graphs[b]
+        gb.replay()
+        return ob
 
     def e2e_run(n):
         copy.wait_stream(comp)
@@ -617,7 +661,7 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
             comp.wait_event(ev_in[b])
             if i >= 2:
                 comp.wait_event(ev_out[b])
-            outs[b] = blk(xs[b])
+            outs[b] = head_step(b)
             ev_done[b].record(comp)
             copy.wait_event(ev_done[b])
             with torch.cuda.stream(copy):
@@ -636,6 +680,10 @@ def run_ep(args, rank, world, local, rb, torch, dist, d, device, hbm_peak, peak_
     tt = torch.tensor([t0.elapsed_time(t1)], device="cuda")
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     e2e_ms = float(tt.item())
+    # Graphs that hold NCCL calls go before the communicators do.
+    head_graphs = g = gout = step = None
+    graphs.clear()
+    torch.cuda.synchronize()
     for _, _, close in made.values():
         close()
     fine_ep = None if args.no_sweep else ep_fine_measure(rb, torch, dist, device, rank, world)
