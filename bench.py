@@ -996,8 +996,9 @@ def stream_model_measure(rb, torch, device, layers=4, batch=16, prompt_len=1024,
     streamer = LayerStreamer(packed, depth=depth, device=device.index or 0)
     max_seq = prompt_len + new_tokens + 3
     resident = D.Decoder(cfg, qw, max_batch=batch, max_seq=max_seq, device=device.index or 0)
-    streamed = D.Decoder(cfg, {k: v for k, v in qw.items() if ".mlp." not in k}, max_batch=batch,
-                         max_seq=max_seq, device=device.index or 0, streamer=streamer)
+    resident_w = {k: v for k, v in qw.items() if ".mlp." not in k}
+    streamed = D.Decoder(cfg, resident_w, max_batch=batch, max_seq=max_seq, device=device.index or 0,
+                         streamer=streamer)
     del qw
     g = torch.Generator().manual_seed(seed)
     prompt = torch.randint(0, cfg.vocab, (batch, prompt_len), generator=g).to(device)
@@ -1029,21 +1030,33 @@ def stream_model_measure(rb, torch, device, layers=4, batch=16, prompt_len=1024,
     h2d = nbytes / (copy_ms / 1000.0) / 1e9 if copy_ms > 0 else 0.0
     s["h2d_gbs"] = round(h2d, 2)
     layer_bytes = packed[0].nbytes
+    streamed.close()
+    streamer.close()
+    # Routed: each decode step routes with resident routers and copies only
+    # the experts its batch routes to (prefills still copy whole layers).
+    routed_st = LayerStreamer(packed, depth=depth, device=device.index or 0, routed=True)
+    routed = D.Decoder(cfg, {k: v for k, v in resident_w.items()}, max_batch=batch, max_seq=max_seq,
+                       device=device.index or 0, streamer=routed_st)
+    rr = run(routed)
+    rb_stats = routed_st.stats()
+    prefill_bytes = 2 * layers * layer_bytes  # warm-up and timed prefills copy whole layers
+    rr["bytes_per_decode_step"] = int((rb_stats["bytes"] - prefill_bytes) / (new_tokens + 1))
+    rr["layer_fraction_copied_per_decode_step"] = round(rr["bytes_per_decode_step"] / (layers * layer_bytes), 3)
+    routed.close()
+    routed_st.close()
     out = {"model": f"mixtral-8x22b shapes, {layers} of 56 layers, synthetic weights (seed {seed}), experts NF4, "
                     "attention/embedding bf16",
            "batch": batch, "prompt_tokens": prompt_len, "new_tokens": new_tokens, "prefetch_buffer_size": depth,
-           "layer_bytes": layer_bytes, "resident": r, "streamed": s,
+           "layer_bytes": layer_bytes, "resident": r, "streamed": s, "streamed_routed": rr,
            "copy_ms_per_layer": round(layer_bytes / h2d / 1e6, 3) if h2d else None,
            "exposed_copy_ms_per_layer_decode": round((s["ms_per_decode_step"] - r["ms_per_decode_step"]) / layers, 3),
            "exposed_copy_ms_per_layer_prefill": round((s["prefill_ms"] - r["prefill_ms"]) / layers, 3),
            "note": "streamed: every forward copies each layer's router + experts from pinned host memory while the "
                    "previous layer computes; resident decode steps are graph replays, streamed ones eager"}
     resident.close()
-    streamed.close()
-    streamer.close()
     for p in packed:
         p.close()
-    del resident, streamed
+    del resident, streamed, routed
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     return out

@@ -156,6 +156,13 @@ int32_t riallm_cuda_streamer_destroy(riallm_streamer* s);
  * at most depth layers ahead); RIALLM_ERR_MEMORY if bytes > slot_bytes. */
 int32_t riallm_cuda_streamer_prefetch(riallm_streamer* s, int32_t layer, const void* host_src,
                                       uint64_t bytes);
+/* The same for n byte ranges of the layer's blob, [offsets[i], offsets[i] +
+ * sizes[i]), each copied to the same offset of the slot (one ready event
+ * for all): a decode step copies only the experts its batch routes to. The
+ * bytes outside the ranges keep whatever the slot held. RIALLM_ERR_MEMORY
+ * if a range leaves the slot. */
+int32_t riallm_cuda_streamer_prefetch_ranges(riallm_streamer* s, int32_t layer, const void* host_src,
+                                             const uint64_t* offsets, const uint64_t* sizes, int32_t n);
 /* Makes `stream` wait for the layer's copy and returns its device address. */
 int32_t riallm_cuda_streamer_acquire(riallm_streamer* s, int32_t layer, void* stream, void** dptr);
 /* Marks the end of the layer's use on `stream` (after its last kernel). */

@@ -137,6 +137,7 @@ SIGNATURES = {
     "riallm_cuda_streamer_create": (_i32, [_vp, _i32, _u64, _vp, ctypes.POINTER(_vp)]),
     "riallm_cuda_streamer_destroy": (_i32, [_vp]),
     "riallm_cuda_streamer_prefetch": (_i32, [_vp, _i32, _vp, _u64]),
+    "riallm_cuda_streamer_prefetch_ranges": (_i32, [_vp, _i32, _vp, _vp, _vp, _i32]),
     "riallm_cuda_streamer_acquire": (_i32, [_vp, _i32, _vp, ctypes.POINTER(_vp)]),
     "riallm_cuda_streamer_release": (_i32, [_vp, _i32, _vp]),
     "riallm_cuda_streamer_stats": (_i32, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64),

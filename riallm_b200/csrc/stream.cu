@@ -141,11 +141,19 @@ int32_t riallm_cuda_streamer_destroy(riallm_streamer* s) {
   return RIALLM_OK;
 }
 
-int32_t riallm_cuda_streamer_prefetch(riallm_streamer* s, int32_t layer, const void* host_src, uint64_t bytes) {
-  if (!s || !host_src || layer < 0) return RIALLM_ERR_INVALID;
-  if (bytes > s->slot_bytes)
-    return fail(s->ctx, RIALLM_ERR_MEMORY, "streamer: layer of " + std::to_string(bytes) +
-                                               " bytes exceeds the slot size " + std::to_string(s->slot_bytes));
+// Copies `n` byte ranges [offsets[i], offsets[i] + sizes[i]) of a layer's
+// host blob to the same offsets of the layer's slot, after the slot's
+// previous layer was released; one timing pair and one ready event for all.
+static int32_t prefetch_ranges(riallm_streamer* s, int32_t layer, const char* host_src, const uint64_t* offsets,
+                               const uint64_t* sizes, int32_t n) {
+  uint64_t total = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    if (offsets[i] > s->slot_bytes || sizes[i] > s->slot_bytes - offsets[i])
+      return fail(s->ctx, RIALLM_ERR_MEMORY, "streamer: range [" + std::to_string(offsets[i]) + ", +" +
+                                                 std::to_string(sizes[i]) + ") exceeds the slot size " +
+                                                 std::to_string(s->slot_bytes));
+    total += sizes[i];
+  }
   const int slot = layer % s->depth;
   if (s->state[slot] == 1 || s->state[slot] == 2)
     return fail(s->ctx, RIALLM_ERR_CONFIG, "streamer: slot of layer " + std::to_string(layer) +
@@ -157,17 +165,34 @@ int32_t riallm_cuda_streamer_prefetch(riallm_streamer* s, int32_t layer, const v
   if (int rc = fold_timing(s, ti)) return rc;
   cudaEvent_t a = s->t_start[ti], b = s->t_stop[ti];
   ST_CUDA(s, cudaEventRecord(a, s->copy), "cudaEventRecord");
-  ST_CUDA(s, cudaMemcpyAsync(s->dev + (uint64_t)slot * s->slot_bytes, host_src, bytes, cudaMemcpyHostToDevice,
-                             s->copy),
-          "streamer H2D");
+  char* dst = s->dev + (uint64_t)slot * s->slot_bytes;
+  for (int32_t i = 0; i < n; ++i)
+    if (sizes[i])
+      ST_CUDA(s, cudaMemcpyAsync(dst + offsets[i], host_src + offsets[i], sizes[i], cudaMemcpyHostToDevice, s->copy),
+              "streamer H2D");
   ST_CUDA(s, cudaEventRecord(b, s->copy), "cudaEventRecord");
   s->t_pending[ti] = 1;
   ST_CUDA(s, cudaEventRecord(s->ready[slot], s->copy), "cudaEventRecord");
   s->layer[slot] = layer;
   s->state[slot] = 1;
-  s->bytes += bytes;
+  s->bytes += total;
   s->copies += 1;
   return RIALLM_OK;
+}
+
+int32_t riallm_cuda_streamer_prefetch(riallm_streamer* s, int32_t layer, const void* host_src, uint64_t bytes) {
+  if (!s || !host_src || layer < 0) return RIALLM_ERR_INVALID;
+  if (bytes > s->slot_bytes)
+    return fail(s->ctx, RIALLM_ERR_MEMORY, "streamer: layer of " + std::to_string(bytes) +
+                                               " bytes exceeds the slot size " + std::to_string(s->slot_bytes));
+  const uint64_t off = 0;
+  return prefetch_ranges(s, layer, static_cast<const char*>(host_src), &off, &bytes, 1);
+}
+
+int32_t riallm_cuda_streamer_prefetch_ranges(riallm_streamer* s, int32_t layer, const void* host_src,
+                                             const uint64_t* offsets, const uint64_t* sizes, int32_t n) {
+  if (!s || !host_src || layer < 0 || n < 0 || (n > 0 && (!offsets || !sizes))) return RIALLM_ERR_INVALID;
+  return prefetch_ranges(s, layer, static_cast<const char*>(host_src), offsets, sizes, n);
 }
 
 int32_t riallm_cuda_streamer_acquire(riallm_streamer* s, int32_t layer, void* stream, void** dptr) {

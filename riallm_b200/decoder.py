@@ -221,6 +221,10 @@ class Decoder:
         self.streamer = streamer
         if streamer is not None and len(streamer.layers) != c.layers:
             raise ConfigError(f"streamer holds {len(streamer.layers)} layers, the model {c.layers}")
+        # A routed streamer's decode steps route with device-resident routers
+        # (E x H per layer, small) and then copy only the routed experts.
+        self.gates = ([pl.tensor("mlp.gate.weight", self.dev) for pl in streamer.layers]
+                      if streamer is not None and streamer.routed else None)
         self.max_batch, self.max_seq = max_batch, max_seq
         shape = (max_batch, c.kv_heads, max_seq, c.head_dim)
         self.k_cache = [torch.zeros(shape, dtype=torch.bfloat16, device=self.dev) for _ in range(c.layers)]
@@ -271,7 +275,8 @@ class Decoder:
         att = torch.empty_like(q)
         L = lib()
         st = self.streamer
-        if st is not None:
+        routed = st is not None and st.routed and T == 1
+        if st is not None and not routed:
             for i in range(min(st.depth, c.layers)):
                 st.prefetch(i)
         for i, layer in enumerate(self.layers):
@@ -286,7 +291,17 @@ class Decoder:
                                                    att.data_ptr(), self._st()))
             o = self._linear(att, layer["wo"])
             self._norm(h, layer["post_norm"], n, delta=o)         # h += o; n = norm(h)
-            moe = layer["moe"] if st is None else st.acquire(i)
+            if st is None:
+                moe = layer["moe"]
+            elif routed:
+                # The experts this step's tokens route to (one host
+                # synchronisation), copied alone into the layer's slot.
+                counts = route(self.gates[i], n, c.top_k, c.experts, ctx=moe_ctx)[2]
+                st.prefetch_experts(i, torch.nonzero(counts > 0).flatten().tolist())
+                moe = dict(st.acquire(i))
+                moe["mlp.gate.weight"] = self.gates[i]
+            else:
+                moe = st.acquire(i)
             if experts_used is not None:
                 counts = route(moe["mlp.gate.weight"], n, c.top_k, c.experts, ctx=moe_ctx)[2]
                 experts_used.append(int((counts > 0).sum().item()))
@@ -296,7 +311,8 @@ class Decoder:
                 apply_moe(moe, n, c.top_k, c.experts, out=h, add_to_out=True, ctx=moe_ctx)
             if st is not None:
                 st.release(i)
-                st.prefetch(i + st.depth)
+                if not routed:
+                    st.prefetch(i + st.depth)
         self.pos[:B].add_(T)
         last = h.view(B, T, -1)[:, -1].contiguous()
         nl = torch.empty_like(last)

@@ -96,6 +96,41 @@ class PackedLayer:
                 out[name] = buf[o:o + n].view(e.dtype).view(e.shape)
         return out
 
+    def expert_ranges(self, experts: Sequence[int], names: Sequence[str] = ("mlp.experts.gate_up_proj",
+                                                                              "mlp.experts.down_proj")):
+        """(offsets, sizes) of the blob bytes that experts `experts` of the
+        quantized [E, ...] tensors `names` occupy: each expert's codes, and
+        its scales and zero points plus the first of the next expert's (the
+        NF4 decode gives element 63 of a block the next block's parameters,
+        and the next block of an expert's last row is the next expert's
+        first)."""
+        offs, sizes = [], []
+        for name in names:
+            e = self.index[name]
+            if e.kind != "q":
+                raise ConfigError(f"{name} is not a quantized tensor")
+            (od, nd), (os_, ns), (oz, nz) = e.parts
+            E = int(e.shape[0])
+            per_d, per_p = nd // E, (ns // 4) // E  # bytes of codes, parameters (f32) per expert
+            for x in sorted(set(int(v) for v in experts)):
+                if not 0 <= x < E:
+                    raise ConfigError(f"expert {x} outside [0, {E})")
+                offs.append(od + x * per_d)
+                sizes.append(per_d)
+                extra = 1 if (x + 1) * per_p < ns // 4 else 0
+                for o in (os_, oz):
+                    offs.append(o + 4 * x * per_p)
+                    sizes.append(4 * (per_p + extra))
+        return offs, sizes
+
+    def tensor(self, name: str, device) -> TensorLike:
+        """One of the layer's tensors copied to `device` (its own memory)."""
+        t = self.views(self.blob)[name]
+        if isinstance(t, QuantizedTensor):
+            return QuantizedTensor(t.data.to(device), t.shape, t.qtype, t.scales.to(device), t.zero_points.to(device),
+                                   t.block_size)
+        return t.to(device)
+
     def close(self):
         if self._hptr is not None:
             self.blob = None
@@ -112,11 +147,15 @@ class LayerStreamer:
 
     or s.run(fn, n) which does exactly that."""
 
-    def __init__(self, layers: Sequence[PackedLayer], depth: int = 2, device: int = 0):
+    def __init__(self, layers: Sequence[PackedLayer], depth: int = 2, device: int = 0, routed: bool = False):
+        """routed: decode steps copy only the experts the step's batch routes
+        to (prefetch_experts, after routing with a device-resident router);
+        prefills and the plain prefetch copy whole layers."""
         if depth < 1:
             raise ConfigError("prefetch_buffer_size must be at least 1")
         self.layers = list(layers)
         self.depth = int(depth)
+        self.routed = bool(routed)
         self.ctx = Context.get(device)
         self.slot_bytes = _align(max(l.nbytes for l in self.layers))
         self.slots = torch.empty(self.depth * self.slot_bytes, dtype=torch.uint8, device=torch.device("cuda", device))
@@ -134,6 +173,17 @@ class LayerStreamer:
             L = lib()
             rc = L.riallm_cuda_streamer_prefetch(self.h, i, self.layers[i].data_ptr(), self.layers[i].nbytes)
             self.ctx.check(rc)
+
+    def prefetch_experts(self, i: int, experts: Sequence[int]):
+        """Copies into layer i's slot only the bytes of experts `experts`
+        (PackedLayer.expert_ranges); the slot's router and other experts are
+        left as they are, so the caller routes with a resident router and
+        runs only these experts."""
+        offs, sizes = self.layers[i].expert_ranges(experts)
+        n = len(offs)
+        o = (ctypes.c_uint64 * max(n, 1))(*offs)
+        z = (ctypes.c_uint64 * max(n, 1))(*sizes)
+        self.ctx.check(lib().riallm_cuda_streamer_prefetch_ranges(self.h, i, self.layers[i].data_ptr(), o, z, n))
 
     def acquire(self, i: int, stream: Optional[torch.cuda.Stream] = None) -> Dict[str, TensorLike]:
         st = (stream or torch.cuda.current_stream()).cuda_stream

@@ -74,3 +74,39 @@ def test_streamer_refuses_misuse(rb):
     s.close()
     for p in packed:
         p.close()
+
+
+def test_routed_streaming_decode_matches_resident(rb):
+    """A decoder whose streamer copies, per decode step, only the experts
+    the step's batch routes to (routers resident) produces the resident
+    decoder's tokens and logits, and copies fewer bytes per step than whole
+    layers. Prefills still copy whole layers."""
+    from riallm_b200 import decoder as D
+    from riallm_b200.streaming import LayerStreamer, PackedLayer
+    cfg = D.DecoderConfig(layers=3)
+    qw = D.synthetic_model(cfg, seed=7, device="cuda")
+    names = ("mlp.gate.weight", "mlp.experts.gate_up_proj", "mlp.experts.down_proj")
+    packed = [PackedLayer({n: qw[f"model.layers.{l}.{n}"] for n in names}) for l in range(cfg.layers)]
+    st = LayerStreamer(packed, depth=2, routed=True)
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab, (2, 20), generator=g).cuda()
+    plain = D.Decoder(cfg, qw, max_batch=2, max_seq=64)
+    t0, l0 = plain.generate(prompt, 5, keep_logits=True)
+    plain.close()
+    dec = D.Decoder(cfg, {k: v for k, v in qw.items() if ".mlp." not in k}, max_batch=2, max_seq=64, streamer=st)
+    b0 = st.stats()["bytes"]
+    dec.forward(prompt)  # prefill: whole layers
+    b1 = st.stats()["bytes"]
+    dec.reset()
+    t1, l1 = dec.generate(prompt, 5, keep_logits=True)
+    b2 = st.stats()["bytes"]
+    dec.close()
+    st.close()
+    full = sum(p.nbytes for p in packed)
+    for p in packed:
+        p.close()
+    assert b1 - b0 == full
+    # generate = one prefill (full layers) + 4 routed decode steps
+    assert b2 - b1 - full < 4 * full
+    assert torch.equal(t0, t1)
+    assert float((l1 - l0).abs().max() / l0.abs().max()) < 1e-5
