@@ -266,10 +266,12 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs
       }
   }
   __syncthreads();
-  if (warp < nt) {
-    const int t = t0 + warp;
-    float* l = lg + warp * E;
-    float* q = pr + warp * E;
+  // One warp per token of the tile (a warp takes several when the tile has
+  // more tokens than the CTA has warps).
+  for (int tw = warp; tw < nt; tw += kRouterThreads / 32) {
+    const int t = t0 + tw;
+    float* l = lg + tw * E;
+    float* q = pr + tw * E;
     float m = __int_as_float(0xff800000);
     for (int e = lane; e < E; e += 32) m = fmaxf(m, l[e]);
 #pragma unroll
