@@ -393,6 +393,7 @@ static int route_into(riallm_ctx* ctx, const riallm_qtensor& gate, const void* x
     a.n_scales = a.n_zeros = 0;
     qtype = RIALLM_COMPRESSION_NONE;
   }
+  a.gate_v8 = qtype == RIALLM_COMPRESSION_NONE && (reinterpret_cast<uintptr_t>(a.gdata) & 31) == 0 ? 1 : 0;
   RL_CUDA(ctx, rl::launch_router(a, qtype, st), "router");
   return RIALLM_OK;
 }

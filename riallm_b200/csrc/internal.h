@@ -157,6 +157,9 @@ struct RouterArgs {
   // and expert, the group's pair count (zeroed before the router runs),
   // then the base of its pairs (router_cta_bytes()).
   int* cta_base;
+  // float32 router weight whose base is 32-byte aligned: each lane reads its
+  // 8-float chunk with one 256-bit load (a warp reads 1 KiB contiguously).
+  int gate_v8;
 };
 // Pairs (T * k) up to which the router's last CTA sorts all pairs by itself;
 // larger calls sort with every router CTA and a scatter kernel.

@@ -70,10 +70,19 @@ __device__ __forceinline__ void load_chunk8(const void* x, bool x_bf16, uint64_t
 template <int QT>
 __device__ __forceinline__ void gate_chunk8(const RouterArgs& a, uint64_t g0, float (&w)[8]) {
   if (QT == RIALLM_COMPRESSION_NONE) {
-    const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(a.gdata) + g0);
-    const float4 u = __ldg(p), v = __ldg(p + 1);
-    w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
-    w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
+    const float* src = reinterpret_cast<const float*>(a.gdata) + g0;
+    if (a.gate_v8) {
+      // One 256-bit load per lane: two 128-bit loads 32 bytes apart would
+      // fetch every 32-byte sector of a warp's 1 KiB twice through L1.
+      asm volatile("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                   : "=f"(w[0]), "=f"(w[1]), "=f"(w[2]), "=f"(w[3]), "=f"(w[4]), "=f"(w[5]), "=f"(w[6]), "=f"(w[7])
+                   : "l"(src));
+    } else {
+      const float4* p = reinterpret_cast<const float4*>(src);
+      const float4 u = __ldg(p), v = __ldg(p + 1);
+      w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+      w[4] = v.x; w[5] = v.y; w[6] = v.z; w[7] = v.w;
+    }
   } else if (QT == RIALLM_COMPRESSION_FOUR_BIT) {
     const uint32_t codes = __ldg(reinterpret_cast<const uint32_t*>(a.gdata) + g0 / 8);
     const uint64_t b0 = g0 >> 6, b7 = (g0 + 8) >> 6;
@@ -221,9 +230,12 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs
     const int t = i / nchunk, c = i - t * nchunk;
     float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (t < nt) load_chunk8(a.x, a.x_bf16 != 0, (uint64_t)(t0 + t) * H + 8ull * c, xv);
-    float* d = xs + (uint64_t)t * H + 8 * c;
+    // A token's row is stored as the first halves of all its chunks, then the
+    // second halves, so the 32 lanes' 16-byte reads of one half are 512
+    // contiguous bytes (no bank conflicts).
+    float* d = xs + (uint64_t)t * H + 4 * c;
     *reinterpret_cast<float4*>(d) = make_float4(xv[0], xv[1], xv[2], xv[3]);
-    *reinterpret_cast<float4*>(d + 4) = make_float4(xv[4], xv[5], xv[6], xv[7]);
+    *reinterpret_cast<float4*>(d + 4 * nchunk) = make_float4(xv[4], xv[5], xv[6], xv[7]);
   }
   __syncthreads();
   for (int e0 = warp * EB; e0 < E; e0 += (kRouterThreads / 32) * EB) {
@@ -246,8 +258,8 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs
       }
 #pragma unroll
       for (int t = 0; t < TT; ++t) {
-        const float4 x0 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 8 * c);
-        const float4 x1 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 8 * c + 4);
+        const float4 x0 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 4 * c);
+        const float4 x1 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 4 * nchunk + 4 * c);
         const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
         for (int j = 0; j < EB; ++j)
