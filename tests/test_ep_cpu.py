@@ -72,9 +72,18 @@ def _worker(rank, world, port, result_dir):
         out = blk(x_local).float().numpy()
         mine = ref[rank * T_LOCAL:(rank + 1) * T_LOCAL]
         err = float(np.abs(out - mine).max() / np.abs(mine).max())
+        # add_to: the block's float32 sum is added to a bf16 residual and
+        # rounded once, in place (the decoder's residual update).
+        g = torch.Generator().manual_seed(40 + rank)
+        resid = torch.randn(T_LOCAL, H, generator=g).to(torch.bfloat16)
+        y32 = blk._forward(x_local, {}, None)
+        want = (resid.float() + y32).to(torch.bfloat16)
+        got = blk(x_local, add_to=resid)
+        same = bool(got is resid and torch.equal(resid, want))
         with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
             f.write(f"{err}\n")
         assert err < 2e-2, err
+        assert same, "add_to must round the float32 sum into the residual once, in place"
     finally:
         dist.destroy_process_group()
 
@@ -161,3 +170,15 @@ def test_exchange_plan_places_rows_expert_major(rb):
     assert cnt.tolist() == [3, 7] and off.tolist() == [0, 3, 10]
     assert pos.tolist() == [[0, 3], [2, 3], [3, 6]]
     assert L.riallm_ep_exchange_plan(0, EL, p(rc), p(cnt), p(off), p(pos)) != 0
+
+
+def test_all_to_all_handle_argument_checks():
+    """The all-to-all handle refuses an unknown transport, and the
+    peer-memory transport without a token capacity, before it touches the
+    process group or the GPU."""
+    from riallm_b200 import ConfigError
+    from riallm_b200.ep import ExpertParallelA2A
+    with pytest.raises(ConfigError, match="transport"):
+        ExpertParallelA2A({}, 8, 2, transport="shm")
+    with pytest.raises(ConfigError, match="max_tokens"):
+        ExpertParallelA2A({}, 8, 2, transport="peer", max_tokens=0)
