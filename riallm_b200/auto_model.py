@@ -222,9 +222,12 @@ class AutoModel:
     @staticmethod
     def from_pretrained(model_id: str, options: Optional[ModelOptions] = None,
                         cache_dir: Optional[str] = None, max_batch: int = 1,
-                        max_seq: Optional[int] = None) -> MoeCausalLM:
+                        max_seq: Optional[int] = None, routed_streaming: bool = False) -> MoeCausalLM:
         """Loads a local Mixtral-architecture checkpoint directory
-        (config.json plus safetensors shards). cache_dir holds the quantized
+        (config.json plus safetensors shards). routed_streaming (with
+        ModelOptions.prefetch_layers; no counterpart in the reference): decode
+        steps copy only the experts their batch routes to, after routing with
+        device-resident routers. cache_dir holds the quantized
         per-layer shards (default: <model_id>/riallm_quantized); max_seq
         defaults to ModelOptions.max_seq_len, else the config's
         max_position_embeddings capped at 4096."""
@@ -277,7 +280,7 @@ class AutoModel:
         if options.prefetch_layers:
             ctx = Context.get(dev)
             packed = [PackedLayer(m, pinned=True, ctx=ctx) for m in moe_layers]
-            streamer = LayerStreamer.from_options(packed, options, dev)
+            streamer = LayerStreamer.from_options(packed, options, dev, routed=routed_streaming)
         else:
             for l, moe in enumerate(moe_layers):
                 for name, t in moe.items():

@@ -165,8 +165,9 @@ class LayerStreamer:
         self.h = h.value
 
     @classmethod
-    def from_options(cls, layers: Sequence[PackedLayer], options: ModelOptions, device: int = 0):
-        return cls(layers, options.prefetch_buffer_size if options.prefetch_layers else 1, device)
+    def from_options(cls, layers: Sequence[PackedLayer], options: ModelOptions, device: int = 0,
+                     routed: bool = False):
+        return cls(layers, options.prefetch_buffer_size if options.prefetch_layers else 1, device, routed)
 
     def prefetch(self, i: int):
         if 0 <= i < len(self.layers):

@@ -78,3 +78,11 @@ def test_from_pretrained_matches_in_memory_model(rb, tmp_path):
     # every forward streams each layer's MoE tensors once: a prefill + 7 decode steps
     assert st["copies"] == 8 * cfg.layers and st["bytes"] > 0
     m.close()
+
+    # Routed streaming: decode steps copy only the experts they route to.
+    m = AutoModel.from_pretrained(str(tmp_path), opts, cache_dir=str(tmp_path / "q"), routed_streaming=True)
+    assert m.streamer.routed
+    assert m.generate(prompt, 8) == want
+    st2 = m.stream_stats()
+    assert st2["copies"] == 8 * cfg.layers and st2["bytes"] < st["bytes"]
+    m.close()
