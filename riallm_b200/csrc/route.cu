@@ -199,6 +199,7 @@ __device__ __forceinline__ void prefetch_share(const void* base, uint64_t bytes)
 // chunks and elements in the same order.
 template <int QT, int TT, int EB>
 __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs a) {
+  static_assert(TT == 1 || TT % 2 == 0, "token tiles of 1 or of whole token pairs");
   extern __shared__ float sm[];
   __shared__ int is_last;
   // The router weight does not depend on the previous kernel: while it
@@ -226,16 +227,36 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs
   // The tile's token rows as float32, staged once (16-byte aligned).
   float* xs = sm + ((2 * TT * E + (kRouterThreads / 32) * (E + 1) + E + 1 + 3) & ~3);
   const int nchunk = H >> 3;
-  for (int i = threadIdx.x; i < TT * nchunk; i += kRouterThreads) {
-    const int t = i / nchunk, c = i - t * nchunk;
-    float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (t < nt) load_chunk8(a.x, a.x_bf16 != 0, (uint64_t)(t0 + t) * H + 8ull * c, xv);
-    // A token's row is stored as the first halves of all its chunks, then the
-    // second halves, so the 32 lanes' 16-byte reads of one half are 512
-    // contiguous bytes (no bank conflicts).
-    float* d = xs + (uint64_t)t * H + 4 * c;
-    *reinterpret_cast<float4*>(d) = make_float4(xv[0], xv[1], xv[2], xv[3]);
-    *reinterpret_cast<float4*>(d + 4 * nchunk) = make_float4(xv[4], xv[5], xv[6], xv[7]);
+  if constexpr (TT == 1) {
+    for (int i = threadIdx.x; i < TT * nchunk; i += kRouterThreads) {
+      const int t = i / nchunk, c = i - t * nchunk;
+      float xv[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (t < nt) load_chunk8(a.x, a.x_bf16 != 0, (uint64_t)(t0 + t) * H + 8ull * c, xv);
+      // The row is stored as the first halves of all its chunks, then the
+      // second halves, so the 32 lanes' 16-byte reads of one half are 512
+      // contiguous bytes (no bank conflicts).
+      float* d = xs + (uint64_t)t * H + 4 * c;
+      *reinterpret_cast<float4*>(d) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+      *reinterpret_cast<float4*>(d + 4 * nchunk) = make_float4(xv[4], xv[5], xv[6], xv[7]);
+    }
+  } else {
+    // Tokens 2u and 2u+1 interleaved: the float4 at xs + ((4u + q) nchunk + c) 4
+    // holds elements 8c+2q and 8c+2q+1 of both, as {x[2u][8c+2q],
+    // x[2u+1][8c+2q], x[2u][8c+2q+1], x[2u+1][8c+2q+1]}, so one read gives
+    // two (token 2u, token 2u+1) operand pairs of the packed FMAs below, and
+    // the 32 lanes' reads of one (u, q) are 512 contiguous bytes. A token
+    // past the tile's end is staged as zeros (its logits are not used).
+    for (int i = threadIdx.x; i < (TT / 2) * nchunk; i += kRouterThreads) {
+      const int u = i / nchunk, c = i - u * nchunk;
+      float xa[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float xb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (2 * u < nt) load_chunk8(a.x, a.x_bf16 != 0, (uint64_t)(t0 + 2 * u) * H + 8ull * c, xa);
+      if (2 * u + 1 < nt) load_chunk8(a.x, a.x_bf16 != 0, (uint64_t)(t0 + 2 * u + 1) * H + 8ull * c, xb);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        *reinterpret_cast<float4*>(xs + ((uint64_t)(4 * u + q) * nchunk + c) * 4) =
+            make_float4(xa[2 * q], xb[2 * q], xa[2 * q + 1], xb[2 * q + 1]);
+    }
   }
   __syncthreads();
   for (int e0 = warp * EB; e0 < E; e0 += (kRouterThreads / 32) * EB) {
@@ -256,15 +277,41 @@ __global__ void __launch_bounds__(kRouterThreads) router_kernel(const RouterArgs
           for (int i = 0; i < 8; ++i) wv[j][i] = 0.0f;
         }
       }
+      if constexpr (TT == 1) {
 #pragma unroll
-      for (int t = 0; t < TT; ++t) {
-        const float4 x0 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 4 * c);
-        const float4 x1 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 4 * nchunk + 4 * c);
-        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        for (int t = 0; t < TT; ++t) {
+          const float4 x0 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 4 * c);
+          const float4 x1 = *reinterpret_cast<const float4*>(xs + (uint64_t)t * H + 4 * nchunk + 4 * c);
+          const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-        for (int j = 0; j < EB; ++j)
+          for (int j = 0; j < EB; ++j)
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[t][j] = __fmaf_rn(xv[i], wv[j][i], acc[t][j]);
+            for (int i = 0; i < 8; ++i) acc[t][j] = __fmaf_rn(xv[i], wv[j][i], acc[t][j]);
+        }
+      } else {
+        // One packed FMA (two independent fused multiply-adds, one rounding
+        // each) advances the chains of tokens 2u and 2u+1 by element i: every
+        // logit still adds its products in element order.
+#pragma unroll
+        for (int u = 0; u < TT / 2; ++u) {
+          float xv[4][4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4*>(xs + ((uint64_t)(4 * u + q) * nchunk + c) * 4);
+            xv[q][0] = v.x;
+            xv[q][1] = v.y;
+            xv[q][2] = v.z;
+            xv[q][3] = v.w;
+          }
+#pragma unroll
+          for (int j = 0; j < EB; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int q = i >> 1, o = (i & 1) * 2;
+              fma_f32x2(acc[2 * u][j], acc[2 * u + 1][j], xv[q][o], xv[q][o + 1], wv[j][i], wv[j][i],
+                        acc[2 * u][j], acc[2 * u + 1][j]);
+            }
+        }
       }
     }
 #pragma unroll
