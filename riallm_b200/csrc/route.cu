@@ -74,7 +74,9 @@ __device__ __forceinline__ void gate_chunk8(const RouterArgs& a, uint64_t g0, fl
     if (a.gate_v8) {
       // One 256-bit load per lane: two 128-bit loads 32 bytes apart would
       // fetch every 32-byte sector of a warp's 1 KiB twice through L1.
-      // Not volatile: a read-only load the compiler may schedule early.
+      // Not volatile, so the compiler may schedule it early within the
+      // chunk loops; those loops start after pdl_wait() and the staging
+      // barrier, and the weight is not written while the kernel runs.
       asm("ld.global.nc.v8.f32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                    : "=f"(w[0]), "=f"(w[1]), "=f"(w[2]), "=f"(w[3]), "=f"(w[4]), "=f"(w[5]), "=f"(w[6]), "=f"(w[7])
                    : "l"(src));
