@@ -34,6 +34,10 @@ def test_router_golden_bit_exact(rb):
     (50, 512, 16, 4, 1, False),     # float32 activations
     (200, 2048, 256, 16, 1, True),  # widest supported: 256 experts, top-16
     (7, 1024, 8, 2, 0, True),       # float32 router weight
+    # One token per CTA with a float32 weight: eight chunks loaded ahead,
+    # several experts per warp, a partial last group of chunks.
+    (64, 2048, 128, 8, 0, True),
+    (45, 1536, 24, 4, 0, False),
     # Prefill sizes: 8 (hidden <= 3072) or 4 tokens per router CTA, a ragged
     # last tile, and above 16384 pairs the multi-CTA pair sort.
     (1001, 2048, 128, 8, 1, True),
