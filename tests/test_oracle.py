@@ -120,6 +120,34 @@ def test_own_expf_accuracy(oracle_lib):
     assert O.expf(-100.0) == 0.0
 
 
+@pytest.mark.parametrize("T,H,E,k,seed", [(512, 4096, 8, 2, 1), (512, 2048, 128, 8, 2)])
+def test_router_softmax_matches_float64(oracle_lib, T, H, E, k, seed):
+    """How far the router's own softmax (own exp, sequential sum in expert
+    order, IEEE division) moves from an exact softmax of the same float32
+    logits: a few float32 ulps in the probabilities, fewer in the
+    renormalised routing weights, and the same top-k set wherever the k-th
+    and (k+1)-th probabilities differ by more than that. (candle's softmax
+    and the order of its logit GEMM are not observable here.)"""
+    O = oracle_lib
+    rng = np.random.default_rng(seed)
+    wg = rng.normal(0, 0.02, (E, H)).astype(np.float32)
+    x = O.synthetic_x(T, H, seed + 10, bf16=True)
+    logits, probs, idx, w = O.router(x, wg, k)
+    l64 = logits.astype(np.float64)
+    p64 = np.exp(l64 - l64.max(axis=1, keepdims=True))
+    p64 /= p64.sum(axis=1, keepdims=True)
+    assert (np.abs(probs - p64) / p64).max() < 2e-6
+    w64 = np.take_along_axis(p64, idx.astype(np.int64), axis=1)
+    w64 /= w64.sum(axis=1, keepdims=True)
+    assert (np.abs(w - w64) / w64).max() < 1e-6
+    top = -np.sort(-p64, axis=1)
+    gap = (top[:, k - 1] - top[:, k]) / top[:, k - 1]
+    exact = np.sort(np.argsort(-p64, axis=1, kind="stable")[:, :k], axis=1)
+    clear = gap > 4e-6
+    assert clear.mean() > 0.99
+    assert np.array_equal(exact[clear], np.sort(idx, axis=1)[clear])
+
+
 def test_router_golden_and_stability(oracle_lib):
     O = oracle_lib
     g = load_golden("router.npz")
